@@ -1,0 +1,431 @@
+#!/usr/bin/env python
+"""Benchmark of the eakv hot path on B200: Q4 decode attention.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 4] [--impl b200|reference]
+
+Metric: "Q4 decode-attention KV tokens/s per GPU; achieved
+HBM GB/s vs B200 peak". One KV token is one cached position of one sequence
+across all layers and KV heads, K and V read once: layers*kv_heads*2*
+(head_dim/64)*40 bytes. A step is one fused decode-attention pass of every
+sequence over every layer (softmax(QK^T/sqrt d)V on the Q4 cache).
+
+Default workload (N=1): config 4 of BASELINE.json, the shape the north-star
+target is quoted on - Llama-3-8B GQA 4:1, 32 layers, 32 Q / 8 KV heads,
+head_dim 128, 32768 cached positions, 16 independent sequences per GPU
+(21.5 GB of Q4 cache per GPU, far above the 126 MB L2, so no flush is
+needed). Under torchrun every rank holds its own 16 sequences (weak scaling,
+no data-path collective); rank 0 prints one JSON line with the whole-job
+throughput and the max-over-ranks step time.
+
+--impl reference times the reference's CPU implementation of the same step
+(reference host C src/cache.c + src/attention.c, compiled from its sources,
+with the C restatement of its Ea kernels) on the host's cores, one sequence
+per thread, on a bounded sample of the workload.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Q4 decode-attention KV tokens/s per GPU; achieved HBM GB/s vs B200 peak"
+UNIT = "KV tokens/s"
+
+CONFIGS = {
+    1: dict(workload="cfg1 README MHA 8/8 heads d128 S2048 B1", L=1, nq=8, nkv=8, hd=128,
+            S=2048, B=1),
+    2: dict(workload="cfg2 TinyLlama-1.1B GQA 8:1 d64 S2048 B1", L=22, nq=32, nkv=4, hd=64,
+            S=2048, B=1),
+    3: dict(workload="cfg3 Llama-2-7B MHA d128 S8192 B1", L=32, nq=32, nkv=32, hd=128,
+            S=8192, B=1),
+    4: dict(workload="cfg4 Llama-3-8B GQA 4:1 d128 S32768 B16", L=32, nq=32, nkv=8, hd=128,
+            S=32768, B=16),
+}
+
+FALLBACK_HBM_GBS = 6650.0
+
+
+def bytes_per_token(c):
+    return c["L"] * c["nkv"] * 2 * (c["hd"] // 64) * 40
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic(kernel_key):
+    """DRAM bytes per KV token of a kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f).get(kernel_key)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.device)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 5:
+                time.sleep(0.02)
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def mark(self):
+        return len(self.lines)
+
+    def stop(self, since=0):
+        if not self.proc:
+            return None
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = [l.split(", ") for l in self.lines[since:] if l.count(",") >= 8]
+        if not rows:
+            rows = [l.split(", ") for l in self.lines if l.count(",") >= 8]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU reference (the reference's own host code + restated kernels)
+
+def cpu_reference(cfg, threads, seconds, seed=0):
+    """KV tokens/s of the reference's two-call path (scores, host softmax,
+    V-sum) run by `threads` host threads, each on its own one-layer cache of
+    the workload's shape. Returns (tokens_per_s, sample description, kind)."""
+    from oracle import oracle as O
+    hd, nq, nkv, S, L = cfg["hd"], cfg["nq"], cfg["nkv"], cfg["S"], cfg["L"]
+    rng = np.random.default_rng(seed)
+    data = rng.standard_normal((1, 2, nkv, S, hd)).astype(np.float32)
+    data[0, 0] *= np.exp(rng.uniform(np.log(0.5), np.log(8.0), (nkv, 1, hd))).astype(np.float32)
+    q = rng.standard_normal(nq * hd).astype(np.float32)
+    use_ref = O.ref_available()
+    caches = []
+    if use_ref:
+        R = O.rlib()
+        for _ in range(threads):
+            c = R.eakv_cache_create(1, nkv, hd, S)
+            assert R.eakv_cache_load_raw(c, data.ctypes.data, S) == 0
+            caches.append(c)
+
+        def unit(c, scores, out):
+            R.eakv_attention_scores(c, q.ctypes.data, 0, nq, nkv, scores.ctypes.data)
+            w = softmax_f32(scores, nq, S)
+            R.eakv_attention_output(c, w.ctypes.data, 0, nq, nkv, out.ctypes.data)
+        kind = "reference"
+    else:
+        for _ in range(threads):
+            rc = O.RefCache(1, nkv, hd, S)
+            rc.load_raw(data, S)
+            caches.append(rc)
+
+        def unit(c, scores, out):
+            s = c.scores(q, 0, nq, nkv)
+            c.output(softmax_f32(s, nq, S), 0, nq, nkv)
+        kind = "port"
+
+    done = [0] * threads
+    stop = threading.Event()
+
+    def worker(i):
+        scores = np.zeros(nq * S, np.float32)
+        out = np.zeros(nq * hd, np.float32)
+        while not stop.is_set():
+            unit(caches[i], scores, out)
+            done[i] += 1
+
+    ths = [threading.Thread(target=worker, args=(i,)) for i in range(threads)]
+    t0 = time.perf_counter()
+    for t in ths:
+        t.start()
+    time.sleep(seconds)
+    stop.set()
+    for t in ths:
+        t.join()
+    dt = time.perf_counter() - t0
+    units = sum(done)
+    if use_ref:
+        for c in caches:
+            O.rlib().eakv_cache_free(c)
+    # L layer-units of one sequence yield S KV tokens
+    tps = units * S / L / dt
+    sample = (f"{units} (sequence, layer) units of {nkv} KV heads x {S} positions "
+              f"(scores + host softmax + V-sum, {threads} thread(s), {dt:.1f} s), "
+              f"scaled by 1/{L} layers per KV token")
+    return tps, sample, kind
+
+
+def softmax_f32(scores, nq, S):
+    s = scores.reshape(nq, S)
+    m = np.maximum(s.max(axis=1, keepdims=True), np.float32(-1e6))
+    e = np.exp(s - m)
+    e /= e.sum(axis=1, keepdims=True)
+    return np.ascontiguousarray(e.reshape(-1), np.float32)
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+# ---------------------------------------------------------------------------
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def run_reference(args, cfg, world, rank):
+    if rank != 0:
+        return
+    threads = host_threads()
+    per_step = []
+    # each step is a bounded sample (about args.cpu_seconds of CPU work on
+    # every thread); the sample count is capped so the run stays short
+    cpu_reference(cfg, threads, 1.0)   # warm-up
+    for _ in range(max(1, min(args.steps, 3))):
+        tps, sample, kind = cpu_reference(cfg, threads, args.cpu_seconds)
+        per_step.append(tps)
+    value = statistics.median(per_step)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": cfg["B"] * cfg["S"] / value * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) K/V, per-channel log-uniform[0.5,8] K scale)",
+        "config": config_json(cfg, world), "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_json(cfg, world):
+    return {"workload": cfg["workload"], "layers": cfg["L"], "q_heads": cfg["nq"],
+            "kv_heads": cfg["nkv"], "head_dim": cfg["hd"], "seq_len": cfg["S"],
+            "batch_per_gpu": cfg["B"], "global_batch": cfg["B"] * world,
+            "parallelism": f"dp{world} (independent sequences per GPU)",
+            "bytes_per_kv_token": bytes_per_token(cfg),
+            "l2": "inputs larger than L2 (Q4 cache >> 126 MB), no flush"}
+
+
+def build_caches(E, torch, cfg, device, seed):
+    """B caches filled with seeded synthetic K/V through the device append
+    path: a pool of 4 K and 4 V slices [kv_heads][S][head_dim] is
+    quantized into every (cache, layer) in rotation."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    H, S, hd, L, B = cfg["nkv"], cfg["S"], cfg["hd"], cfg["L"], cfg["B"]
+    P = 4
+    kpool, vpool = [], []
+    for _ in range(P):
+        ch = torch.exp(torch.empty(H, 1, hd, device=device).uniform_(np.log(0.5), np.log(8.0),
+                                                                     generator=g))
+        kpool.append((torch.randn(H, S, hd, device=device, generator=g) * ch).contiguous())
+        vpool.append(torch.randn(H, S, hd, device=device, generator=g).contiguous())
+    torch.cuda.synchronize()
+    caches = []
+    for b in range(B):
+        c = E.Cache(L, H, hd, S)
+        for l in range(L):
+            assert c.append_device(kpool[(b + l) % P], l, 0, S) == 0
+            assert c.append_device(vpool[(b + 3 * l + 1) % P], l, 1, S) == 0
+        c.synchronize()
+        assert c.advance(S) == 0
+        caches.append(c)
+    del kpool, vpool
+    torch.cuda.empty_cache()
+    return caches
+
+
+def run_b200(args, cfg, world, rank, local):
+    import torch
+    import eakv_b200 as E
+    torch.cuda.set_device(local)
+    E.set_device(local)
+    dev = torch.device("cuda", local)
+    caches = build_caches(E, torch, cfg, dev, seed=1234 + rank)
+    B, L, nq, hd = cfg["B"], cfg["L"], cfg["nq"], cfg["hd"]
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+    qs = [torch.randn(B, L, nq, hd, device=dev) for _ in range(4)]
+    out = torch.empty(B, L, nq, hd, device=dev)
+    launches_per_step = E.decode_launches(caches, nq)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world > 1:
+            import torch.distributed as dist
+            t = torch.tensor([x], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+        return x
+
+    for i in range(args.warmup):
+        E.decode_attention(caches, qs[i % 4], nq, out, stream=sh)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    mark = clocks.mark()
+    torch.cuda.synchronize()
+    barrier()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    evs[0].record(stream)
+    for i in range(args.steps):
+        E.decode_attention(caches, qs[i % 4], nq, out, stream=sh)
+        evs[i + 1].record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop(mark)
+    per = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    total_ms = evs[0].elapsed_time(evs[-1])
+    ms_step = max_over_ranks(total_ms / args.steps)
+    avg_launch_ms = max_over_ranks(sum(per) / len(per))
+    status = E.device_status(local)
+
+    # end to end: host (pinned) queries in, host output back, every step
+    qh = torch.randn(B, L, nq, hd, pin_memory=True).numpy()
+    oh = torch.empty(B, L, nq, hd, pin_memory=True).numpy()
+    for _ in range(2):
+        E.decode_attention_host(caches, qh, nq, oh, stream=sh)
+    torch.cuda.synchronize()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        E.decode_attention_host(caches, qh, nq, oh, stream=sh)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    assert np.isfinite(oh).all()
+
+    tokens_step = B * cfg["S"] * world
+    value = tokens_step / (ms_step / 1e3)
+    bpt = bytes_per_token(cfg)
+    alg_bytes_launch = B * cfg["S"] * bpt   # one decode launch per rank covers all of it
+    peak, peak_kind = measured_peak()
+    achieved = alg_bytes_launch / (avg_launch_ms / 1e3) / 1e9
+    traffic_per_token = ncu_traffic(f"decode_simt_kernel<{hd},{min(8, nq // cfg['nkv'])}>")
+    result = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            tps, sample, kind = cpu_reference(cfg, 1, args.cpu_seconds)
+            cpu = {"value": tps, "unit": UNIT, "cores": 1, "kind": kind, "sample": sample}
+        result = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded torch.randn K/V on device, per-channel log-uniform[0.5,8] "
+                    "K scale, 4-slice pool rotated over caches/layers)",
+            "config": config_json(cfg, world),
+            "e2e": {"value": tokens_step / (e2e_ms / 1e3), "unit": UNIT,
+                    "h2d_bytes_per_step": int(qh.nbytes), "d2h_bytes_per_step": int(oh.nbytes),
+                    "api": "eakv_decode_attention_host"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                         "traffic": (traffic_per_token * B * cfg["S"]) if traffic_per_token
+                         else None,
+                         "kernel": f"decode_simt_kernel<{hd},{min(8, nq // cfg['nkv'])}>",
+                         "algorithmic_bytes_per_launch": alg_bytes_launch},
+            "cpu_baseline": cpu,
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+            "device_status": status,
+        }
+        print(json.dumps(result), flush=True)
+    for c in caches:
+        c.free()
+    return result
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", type=int, default=4, choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    cfg = CONFIGS[args.config]
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        if args.impl == "reference":
+            run_reference(args, cfg, world, rank)
+        else:
+            run_b200(args, cfg, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,294 @@
+// api.cu - extension entry points of eakv_cuda.h: fused attention (single
+// layer and batched decode step), sequence-split partials, the exact
+// log-sum-exp combine, and the device status word.
+#include <math.h>
+#include <string.h>
+
+#include "internal.cuh"
+
+namespace eakv {
+
+// Sticky status word of the library's kernels (one per device).
+__device__ int g_status;
+
+// Split count forced by eakv_test_force_splits() on this host thread.
+thread_local int t_force_splits = 0;
+
+int *device_status_ptr() {
+  static int *ptrs[64] = {nullptr};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (!ptrs[dev]) {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_status) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    ptrs[dev] = (int *)p;
+  }
+  return ptrs[dev];
+}
+
+}  // namespace eakv
+
+using namespace eakv;
+
+namespace {
+
+int check_batch(const eakv_cache_t *const *caches, int n, int n_q, const char *who) {
+  if (!caches || n <= 0 || n > kMaxBatch) {
+    set_error(EAKV_ERR_INVALID, "%s: need 1..%d caches", who, kMaxBatch);
+    return EAKV_ERR_INVALID;
+  }
+  const eakv_cache_t *c0 = caches[0];
+  if (!c0) {
+    set_error(EAKV_ERR_INVALID, "%s: NULL cache", who);
+    return EAKV_ERR_INVALID;
+  }
+  if (c0->head_dim != 64 && c0->head_dim != 128) {
+    set_error(EAKV_ERR_INVALID, "%s: head_dim %d unsupported (64 or 128)", who, c0->head_dim);
+    return EAKV_ERR_INVALID;
+  }
+  if (n_q < c0->n_kv_heads || n_q % c0->n_kv_heads != 0) {
+    set_error(EAKV_ERR_INVALID, "%s: n_q_heads %d not a multiple of n_kv_heads %d", who, n_q,
+              c0->n_kv_heads);
+    return EAKV_ERR_INVALID;
+  }
+  for (int i = 1; i < n; i++) {
+    const eakv_cache_t *c = caches[i];
+    if (!c || c->n_layers != c0->n_layers || c->n_kv_heads != c0->n_kv_heads ||
+        c->head_dim != c0->head_dim || c->max_seq_len != c0->max_seq_len ||
+        c->device != c0->device) {
+      set_error(EAKV_ERR_INVALID, "%s: cache %d differs in shape or device", who, i);
+      return EAKV_ERR_INVALID;
+    }
+  }
+  return EAKV_OK;
+}
+
+DecodeArgs base_args(const eakv_cache_t *c0, int n_caches, int n_q) {
+  DecodeArgs a;
+  memset(&a, 0, sizeof a);
+  a.geom = c0->geom;
+  a.head_dim = c0->head_dim;
+  a.n_caches = n_caches;
+  a.n_q_heads = n_q;
+  a.layer0 = 0;
+  a.n_layers = c0->n_layers;
+  a.pos_begin = 0;
+  a.pos_end = -1;
+  a.status = device_status_ptr();
+  a.force_splits = t_force_splits;
+  return a;
+}
+
+void fill_batch(DecodeBatch &b, const eakv_cache_t *const *caches, int n) {
+  for (int i = 0; i < n; i++) {
+    b.base[i] = caches[i]->d_buf;
+    b.seq_len[i] = caches[i]->seq_len;
+  }
+}
+
+// Runs the decode with workspace from the first cache's scratch, placed
+// after `reserve` bytes the caller already uses there.
+int run_decode(const eakv_cache_t *c0, DecodeArgs &a, const DecodeBatch &b, size_t reserve,
+               cudaStream_t s) {
+  size_t ws = decode_workspace_bytes(a, b);
+  void *w = nullptr;
+  if (ws) {
+    uint8_t *base = (uint8_t *)cache_scratch(c0, reserve + ws);
+    if (!base) return EAKV_ERR_ALLOC;
+    w = base + reserve;
+  }
+  return decode_launch(a, b, w, ws, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+int eakv_device_status(int device, int reset) {
+  clear_error();
+  DeviceGuard g(device);
+  int *p = device_status_ptr();
+  if (!p) {
+    set_error(EAKV_ERR_INVALID, "device_status: symbol lookup failed");
+    return EAKV_ERR_INVALID;
+  }
+  int v = 0;
+  int rc = check_cuda(cudaDeviceSynchronize(), "device_status");
+  if (rc) return rc;
+  rc = check_cuda(cudaMemcpy(&v, p, sizeof v, cudaMemcpyDeviceToHost), "device_status");
+  if (rc) return rc;
+  if (reset) {
+    int z = 0;
+    rc = check_cuda(cudaMemcpy(p, &z, sizeof z, cudaMemcpyHostToDevice), "device_status");
+    if (rc) return rc;
+  }
+  return v;
+}
+
+int eakv_attention_fused_device(const eakv_cache_t *c, const float *d_q, int layer, int n_q,
+                                int n_kv, float *d_out) {
+  clear_error();
+  if (!c || !d_q || !d_out || layer < 0 || layer >= c->n_layers || n_kv != c->n_kv_heads) {
+    set_error(EAKV_ERR_INVALID, "attention_fused: invalid argument");
+    return EAKV_ERR_INVALID;
+  }
+  const eakv_cache_t *cs[1] = {c};
+  int rc = check_batch(cs, 1, n_q, "attention_fused");
+  if (rc) return rc;
+  DeviceGuard g(c->device);
+  DecodeArgs a = base_args(c, 1, n_q);
+  a.layer0 = layer;
+  a.n_layers = 1;
+  a.q = d_q;
+  a.out = d_out;
+  DecodeBatch b;
+  fill_batch(b, cs, 1);
+  return run_decode(c, a, b, 0, c->stream);
+}
+
+int eakv_attention_fused(const eakv_cache_t *c, const float *queries, int layer, int n_q,
+                         int n_kv, float *output) {
+  clear_error();
+  if (!c || !queries || !output || layer < 0 || layer >= c->n_layers || n_kv != c->n_kv_heads) {
+    set_error(EAKV_ERR_INVALID, "attention_fused: invalid argument");
+    return EAKV_ERR_INVALID;
+  }
+  const eakv_cache_t *cs[1] = {c};
+  int rc = check_batch(cs, 1, n_q, "attention_fused");
+  if (rc) return rc;
+  DeviceGuard g(c->device);
+  const size_t n = (size_t)n_q * c->head_dim;
+  const size_t reserve = 2 * ((n * sizeof(float) + 255) / 256 * 256);
+  DecodeArgs a = base_args(c, 1, n_q);
+  a.layer0 = layer;
+  a.n_layers = 1;
+  DecodeBatch b;
+  fill_batch(b, cs, 1);
+  size_t ws = decode_workspace_bytes(a, b);
+  uint8_t *base = (uint8_t *)cache_scratch(c, reserve + ws);
+  if (!base) return EAKV_ERR_ALLOC;
+  float *d_q = (float *)base;
+  float *d_o = (float *)(base + reserve / 2);
+  a.q = d_q;
+  a.out = d_o;
+  rc = check_cuda(cudaMemcpyAsync(d_q, queries, n * sizeof(float), cudaMemcpyHostToDevice,
+                                  c->stream), "attention_fused: copy");
+  if (rc) return rc;
+  rc = decode_launch(a, b, ws ? base + reserve : nullptr, ws, c->stream);
+  if (rc) return rc;
+  rc = check_cuda(cudaMemcpyAsync(output, d_o, n * sizeof(float), cudaMemcpyDeviceToHost,
+                                  c->stream), "attention_fused: copy");
+  if (rc) return rc;
+  return check_cuda(cudaStreamSynchronize(c->stream), "attention_fused");
+}
+
+int eakv_decode_attention(const eakv_cache_t *const *caches, int n_caches, const float *d_q,
+                          int n_q, float *d_out, void *stream) {
+  clear_error();
+  int rc = check_batch(caches, n_caches, n_q, "decode_attention");
+  if (rc) return rc;
+  if (!d_q || !d_out) {
+    set_error(EAKV_ERR_INVALID, "decode_attention: NULL buffer");
+    return EAKV_ERR_INVALID;
+  }
+  const eakv_cache_t *c0 = caches[0];
+  DeviceGuard g(c0->device);
+  cudaStream_t s = stream ? (cudaStream_t)stream : c0->stream;
+  DecodeArgs a = base_args(c0, n_caches, n_q);
+  a.q = d_q;
+  a.out = d_out;
+  DecodeBatch b;
+  fill_batch(b, caches, n_caches);
+  return run_decode(c0, a, b, 0, s);
+}
+
+int eakv_decode_launches(const eakv_cache_t *const *caches, int n_caches, int n_q) {
+  clear_error();
+  int rc = check_batch(caches, n_caches, n_q, "decode_launches");
+  if (rc) return rc;
+  DeviceGuard g(caches[0]->device);
+  DecodeArgs a = base_args(caches[0], n_caches, n_q);
+  DecodeBatch b;
+  fill_batch(b, caches, n_caches);
+  return decode_workspace_bytes(a, b) ? 2 : 1;
+}
+
+int eakv_decode_attention_host(const eakv_cache_t *const *caches, int n_caches,
+                               const float *queries, int n_q, float *output, void *stream) {
+  clear_error();
+  int rc = check_batch(caches, n_caches, n_q, "decode_attention_host");
+  if (rc) return rc;
+  if (!queries || !output) {
+    set_error(EAKV_ERR_INVALID, "decode_attention_host: NULL buffer");
+    return EAKV_ERR_INVALID;
+  }
+  const eakv_cache_t *c0 = caches[0];
+  DeviceGuard g(c0->device);
+  cudaStream_t s = stream ? (cudaStream_t)stream : c0->stream;
+  const size_t n = (size_t)n_caches * c0->n_layers * n_q * c0->head_dim;
+  const size_t half = (n * sizeof(float) + 255) / 256 * 256;
+  DecodeArgs a = base_args(c0, n_caches, n_q);
+  DecodeBatch b;
+  fill_batch(b, caches, n_caches);
+  size_t ws = decode_workspace_bytes(a, b);
+  uint8_t *base = (uint8_t *)cache_scratch(c0, 2 * half + ws);
+  if (!base) return EAKV_ERR_ALLOC;
+  a.q = (float *)base;
+  a.out = (float *)(base + half);
+  rc = check_cuda(cudaMemcpyAsync((void *)a.q, queries, n * sizeof(float),
+                                  cudaMemcpyHostToDevice, s), "decode_attention_host: copy");
+  if (rc) return rc;
+  rc = decode_launch(a, b, ws ? base + 2 * half : nullptr, ws, s);
+  if (rc) return rc;
+  rc = check_cuda(cudaMemcpyAsync(output, a.out, n * sizeof(float), cudaMemcpyDeviceToHost, s),
+                  "decode_attention_host: copy");
+  if (rc) return rc;
+  return check_cuda(cudaStreamSynchronize(s), "decode_attention_host");
+}
+
+int eakv_decode_attention_partial(const eakv_cache_t *const *caches, int n_caches,
+                                  const float *d_q, int n_q, int pos_begin, int pos_end,
+                                  float *d_out, float *d_lse, void *stream) {
+  clear_error();
+  int rc = check_batch(caches, n_caches, n_q, "decode_attention_partial");
+  if (rc) return rc;
+  if (!d_q || !d_out || !d_lse || pos_begin < 0 || (pos_end >= 0 && pos_end < pos_begin)) {
+    set_error(EAKV_ERR_INVALID, "decode_attention_partial: invalid argument");
+    return EAKV_ERR_INVALID;
+  }
+  const eakv_cache_t *c0 = caches[0];
+  DeviceGuard g(c0->device);
+  cudaStream_t s = stream ? (cudaStream_t)stream : c0->stream;
+  DecodeArgs a = base_args(c0, n_caches, n_q);
+  a.q = d_q;
+  a.out = d_out;
+  a.lse = d_lse;
+  a.pos_begin = pos_begin;
+  a.pos_end = pos_end;
+  DecodeBatch b;
+  fill_batch(b, caches, n_caches);
+  return run_decode(c0, a, b, 0, s);
+}
+
+int eakv_lse_combine(int n_parts, int n_rows, int head_dim, const float *d_parts,
+                     const float *d_lse, float *d_out, float *d_lse_out, void *stream) {
+  clear_error();
+  if (n_parts <= 0 || n_rows < 0 || head_dim <= 0 || head_dim > 1024 || !d_parts || !d_lse ||
+      !d_out) {
+    set_error(EAKV_ERR_INVALID, "lse_combine: invalid argument");
+    return EAKV_ERR_INVALID;
+  }
+  return lse_combine_launch(n_parts, n_rows, head_dim, d_parts, d_lse, d_out, d_lse_out,
+                            (cudaStream_t)stream);
+}
+
+}  // extern "C"
+
+extern "C" int eakv_test_force_splits(int n) {
+  eakv::t_force_splits = n > 0 ? n : 0;
+  return EAKV_OK;
+}

@@ -1,0 +1,138 @@
+// internal.cuh - device layout of the Q4 cache, the cache object, and the
+// launch interfaces shared by the .cu files of libeakv_b200.so.
+//
+// Device layout ("pages"). The reference keeps, per (layer, K/V), one flat
+// block [nibbles][scales][biases] with a head stride of max_seq_len*hd/64
+// groups (reference src/cache.c:37-48, src/internal.h:8-26). Here the same
+// data is cut into PAGES of 64 consecutive positions of one head of one
+// (layer, K/V):
+//
+//   page = [ nibbles : 64 * gpd * 32 bytes, row-major [position][group][32] ]
+//          [ sb      : 64 * gpd float2 (scale, bias), [position][group]    ]
+//
+// with gpd = head_dim/64 groups per position. A page is 64*gpd*40 bytes
+// (2560 B at hd 64, 5120 B at hd 128), every page starts 16-byte aligned,
+// and pages are ordered [layer][kv][head][page]. One page is therefore a
+// single contiguous bulk copy for the tensor memory accelerator, a
+// position's nibble row is contiguous (64 B at hd 128), and the (scale,
+// bias) of a group is one 8-byte load. The split-nibble packing of a group
+// is unchanged: byte k holds element k (low nibble) and element k+32 (high
+// nibble) (reference kernels/quantize_simd.ea:3-7).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stddef.h>
+
+#include "../../include/eakv.h"
+#include "../../include/eakv_cuda.h"
+
+namespace eakv {
+
+constexpr int kPagePositions = 64;
+constexpr int kGroup = 64;
+
+struct PageGeom {
+  int gpd;              // groups per position per head (head_dim / 64)
+  int n_pages;          // pages per (layer, kv, head)
+  int n_heads;          // KV heads
+  int n_layers;
+  uint32_t nib_bytes;   // nibble bytes of one page
+  uint32_t page_bytes;  // nibbles + (scale, bias) pairs of one page
+};
+
+__host__ __device__ inline size_t page_index(const PageGeom &g, int layer, int kv,
+                                             int head, int page) {
+  return ((((size_t)layer * 2 + kv) * g.n_heads + head) * g.n_pages + page);
+}
+
+}  // namespace eakv
+
+struct eakv_cache {
+  int n_layers;
+  int n_kv_heads;
+  int head_dim;
+  int max_seq_len;
+  int seq_len;
+  eakv::PageGeom geom;
+  uint8_t *d_buf;       // device slab, geom-ordered pages
+  size_t buf_bytes;
+  int device;
+  cudaStream_t stream;
+  int own_stream;
+  // grow-on-demand device scratch for the host-pointer entry points
+  mutable void *d_scratch;
+  mutable size_t scratch_bytes;
+};
+
+namespace eakv {
+
+// Thread-local error record behind eakv_last_error().
+void set_error(int code, const char *fmt, ...);
+void clear_error();
+int check_cuda(cudaError_t e, const char *what);   // EAKV_OK or EAKV_ERR_*
+
+// Makes the cache's device current for the lifetime of the guard.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+void *cache_scratch(const eakv_cache *c, size_t bytes);   // nullptr on failure
+
+// ---- quantize.cu ----
+// Quantizes n_units units of n_tok*head_dim floats each: the n_tok*gpd
+// groups of unit u go to unit (unit_base + u) at positions pos0.., where a
+// unit is one (layer, kv, head) triple in [layer][kv][head] order.
+cudaError_t launch_quantize(const PageGeom &g, uint8_t *d_buf, const float *d_src,
+                            int head_dim, int unit_base, int n_units, int n_tok, int pos0,
+                            cudaStream_t s);
+
+// ---- attention.cu (two-call API) ----
+cudaError_t launch_scores(const PageGeom &g, const uint8_t *d_buf, int layer,
+                          const float *d_q, int n_q, int n_kv, int seq_len,
+                          float rsqrt_d, float *d_scores, cudaStream_t s);
+cudaError_t launch_vsum(const PageGeom &g, const uint8_t *d_buf, int layer,
+                        const float *d_w, int n_q, int n_kv, int seq_len,
+                        float *d_out, float *d_part, size_t part_floats,
+                        cudaStream_t s);
+size_t vsum_scratch_floats(const PageGeom &g, int n_q, int seq_len);
+
+// ---- decode.cu (fused flash-decoding) ----
+constexpr int kMaxBatch = 256;
+struct DecodeBatch {
+  const uint8_t *base[kMaxBatch];   // device slab of each cache
+  int seq_len[kMaxBatch];           // positions to attend per cache
+};
+struct DecodeArgs {
+  PageGeom geom;
+  int head_dim;
+  int n_caches;
+  int n_q_heads;
+  int layer0, n_layers;             // layers [layer0, layer0 + n_layers)
+  int pos_begin, pos_end;           // attended range clamp (pos_end < 0: up to seq_len)
+  const float *q;                   // [cache][layer][q_head][head_dim]
+  float *out;                       // same shape as q (normalized output)
+  float *lse;                       // optional [cache][layer][q_head] natural-log LSE
+  int *status;                      // device status word (bounded waits)
+  int force_splits;                 // > 0: use this many splits (tests)
+  // filled by the planner
+  int n_splits, split_pages;
+  float *part_m, *part_l, *part_o;
+};
+int decode_launch(const DecodeArgs &a, const DecodeBatch &batch, void *workspace,
+                  size_t workspace_bytes, cudaStream_t s);
+size_t decode_workspace_bytes(const DecodeArgs &a, const DecodeBatch &batch);
+int lse_combine_launch(int n_parts, int n_rows, int head_dim, const float *parts,
+                       const float *lse, float *out, float *lse_out, cudaStream_t s);
+int *device_status_ptr();   // status word of the current device
+extern thread_local int t_force_splits;
+
+}  // namespace eakv
