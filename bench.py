@@ -300,10 +300,16 @@ def run_b200(args, cfg, world, rank, local):
     import eakv_b200 as E
     torch.cuda.set_device(local)
     E.set_device(local)
+    if args.force_simt:
+        E.force_path(1)
     dev = torch.device("cuda", local)
     caches = build_caches(E, torch, cfg, dev, seed=1234 + rank)
     B, L, nq, hd = cfg["B"], cfg["L"], cfg["nq"], cfg["hd"]
-    stream = torch.cuda.current_stream(dev)
+    # a stream of our own: the legacy default stream has handle 0, which the
+    # library reads as "the cache's stream"; events must sit on the stream
+    # the kernels run on
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
     sh = stream.cuda_stream
     qs = [torch.randn(B, L, nq, hd, device=dev) for _ in range(4)]
     out = torch.empty(B, L, nq, hd, device=dev)
@@ -368,7 +374,13 @@ def run_b200(args, cfg, world, rank, local):
     alg_bytes_launch = B * cfg["S"] * bpt   # one decode launch per rank covers all of it
     peak, peak_kind = measured_peak()
     achieved = alg_bytes_launch / (avg_launch_ms / 1e3) / 1e9
-    traffic_per_token = ncu_traffic(f"decode_simt_kernel<{hd},{min(8, nq // cfg['nkv'])}>")
+    G = nq // cfg["nkv"]
+    if not args.force_simt and hd in (64, 128) and G % 4 == 0:
+        kname = f"decode_mma_kernel<{hd},{8 if G % 8 == 0 else 4}>"
+    else:
+        gc = 8 if G % 8 == 0 else 4 if G % 4 == 0 else 2 if G % 2 == 0 else 1
+        kname = f"decode_simt_kernel<{hd},{gc}>"
+    traffic_per_token = ncu_traffic(kname)
     result = None
     if rank == 0:
         cpu = None
@@ -389,7 +401,7 @@ def run_b200(args, cfg, world, rank, local):
                          "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
                          "traffic": (traffic_per_token * B * cfg["S"]) if traffic_per_token
                          else None,
-                         "kernel": f"decode_simt_kernel<{hd},{min(8, nq // cfg['nkv'])}>",
+                         "kernel": kname,
                          "algorithmic_bytes_per_launch": alg_bytes_launch},
             "cpu_baseline": cpu,
             "gpu_launches": launches_per_step * args.steps,
@@ -411,10 +423,21 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override sequences per GPU (smaller cases for profiling)")
+    ap.add_argument("--seq", type=int, default=0, help="override cached positions")
+    ap.add_argument("--force-simt", action="store_true",
+                    help="time the CUDA-core decode kernel even where tensor cores apply")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.batch:
+        cfg["B"] = args.batch
+        cfg["workload"] += f" (batch overridden to {args.batch})"
+    if args.seq:
+        cfg["S"] = args.seq
+        cfg["workload"] += f" (seq_len overridden to {args.seq})"
     world, rank, local = dist_setup(args.gpus)
     try:
         if args.impl == "reference":

@@ -76,6 +76,7 @@ SIGNATURES = {
     "eakv_decode_attention_partial": (_I, [_P, _I, _P, _I, _I, _I, _P, _P, _P]),
     "eakv_lse_combine": (_I, [_I, _I, _I, _P, _P, _P, _P, _P]),
     "eakv_test_force_splits": (_I, [_I]),
+    "eakv_test_force_path": (_I, [_I]),
 }
 
 _lib = None
@@ -314,3 +315,8 @@ def device_status(device=0, reset=False):
 
 def force_splits(n):
     lib().eakv_test_force_splits(int(n))
+
+
+def force_path(path):
+    """1: CUDA-core decode kernel for every shape; 0: automatic choice."""
+    lib().eakv_test_force_path(int(path))

@@ -13,6 +13,8 @@ __device__ int g_status;
 
 // Split count forced by eakv_test_force_splits() on this host thread.
 thread_local int t_force_splits = 0;
+// Kernel path forced by eakv_test_force_path() on this host thread.
+thread_local int t_force_path = 0;
 
 int *device_status_ptr() {
   static int *ptrs[64] = {nullptr};
@@ -80,6 +82,7 @@ DecodeArgs base_args(const eakv_cache_t *c0, int n_caches, int n_q) {
   a.pos_end = -1;
   a.status = device_status_ptr();
   a.force_splits = t_force_splits;
+  a.force_path = t_force_path;
   return a;
 }
 
@@ -287,6 +290,11 @@ int eakv_lse_combine(int n_parts, int n_rows, int head_dim, const float *d_parts
 }
 
 }  // extern "C"
+
+extern "C" int eakv_test_force_path(int path) {
+  eakv::t_force_path = path == 1 ? 1 : 0;
+  return EAKV_OK;
+}
 
 extern "C" int eakv_test_force_splits(int n) {
   eakv::t_force_splits = n > 0 ? n : 0;

@@ -25,12 +25,11 @@
 
 #include "internal.cuh"
 #include "pipeline.cuh"
+#include "decode_common.cuh"
 
 namespace eakv {
 namespace {
 
-constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kLn2 = 0.6931471805599453f;
 
 template <int HD, int GC>
 struct Cfg {
@@ -56,11 +55,6 @@ struct Cfg {
   static_assert(32 % BPL == 0, "a lane's bytes stay within one group");
 };
 
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 
 // 8 nibbles of a 32-bit word -> floats: low nibbles of bytes 0..3 and high
 // nibbles of bytes 0..3, exact. Each byte is placed in the mantissa of 2^23
@@ -98,32 +92,6 @@ __device__ __forceinline__ void convert(const uint32_t (&w)[BPL / 4], float2 (&n
                                         float2 (&nh)[BPL / 2]) {
 #pragma unroll
   for (int m = 0; m < BPL / 4; m++) nib8(w[m], nl[2 * m], nl[2 * m + 1], nh[2 * m], nh[2 * m + 1]);
-}
-
-struct Item {
-  int b, layer, lrow, h, hg, split;
-  int r0, r1;       // attended positions [r0, r1)
-  int pg0, npages;  // pages of this split
-};
-
-__device__ __forceinline__ Item decode_item(const DecodeArgs &a, const DecodeBatch &batch, int nhg) {
-  Item it;
-  int bid = blockIdx.x;
-  it.split = bid % a.n_splits; bid /= a.n_splits;
-  it.hg = bid % nhg; bid /= nhg;
-  it.h = bid % a.geom.n_heads; bid /= a.geom.n_heads;
-  it.lrow = bid % a.n_layers;
-  it.b = bid / a.n_layers;
-  it.layer = a.layer0 + it.lrow;
-  const int seq = batch.seq_len[it.b];
-  it.r0 = a.pos_begin > 0 ? a.pos_begin : 0;
-  it.r1 = a.pos_end < 0 ? seq : min(seq, a.pos_end);
-  int P0 = it.r0 / kPagePositions;
-  int P1 = it.r1 > it.r0 ? (it.r1 + kPagePositions - 1) / kPagePositions : P0;
-  it.pg0 = P0 + it.split * a.split_pages;
-  int pg1 = min(P1, it.pg0 + a.split_pages);
-  it.npages = pg1 > it.pg0 ? pg1 - it.pg0 : 0;
-  return it;
 }
 
 template <int HD, int GC>
@@ -494,11 +462,20 @@ int resident_gc(int gc) {
 
 }  // namespace
 
-// Chooses the split count: enough CTAs for ~8 waves of resident blocks, at
-// least one page per split.
-static void plan(DecodeArgs &a, const DecodeBatch &batch, int *n_items_out) {
+// Chooses the kernel (tensor cores for GQA groups of 4 or 8 query heads per
+// KV head, CUDA cores otherwise) and the split count: enough CTAs for ~8
+// waves of resident blocks, at least one page per split.
+struct Plan {
+  int mma_gh;   // 0: CUDA-core kernel
+  int gc;       // query heads per CTA
+  int items;
+};
+
+static Plan plan(DecodeArgs &a, const DecodeBatch &batch) {
   const int G = a.n_q_heads / a.geom.n_heads;
-  const int gc = pick_gc(G);
+  Plan p;
+  p.mma_gh = a.force_path == 1 ? 0 : mma_heads_per_cta(G, a.head_dim);
+  p.gc = p.mma_gh ? p.mma_gh : pick_gc(G);
   int max_pages = 0;
   for (int i = 0; i < a.n_caches; i++) {
     int r0 = a.pos_begin > 0 ? a.pos_begin : 0;
@@ -506,25 +483,25 @@ static void plan(DecodeArgs &a, const DecodeBatch &batch, int *n_items_out) {
     int pages = r1 > r0 ? (r1 + kPagePositions - 1) / kPagePositions - r0 / kPagePositions : 0;
     if (pages > max_pages) max_pages = pages;
   }
-  const int items = a.n_caches * a.n_layers * a.geom.n_heads * (G / gc);
-  const int resident = a.head_dim == 128 ? resident_gc<128>(gc) : resident_gc<64>(gc);
+  p.items = a.n_caches * a.n_layers * a.geom.n_heads * (G / p.gc);
+  const int resident = p.mma_gh ? mma_resident(p.mma_gh, a.head_dim)
+                                : (a.head_dim == 128 ? resident_gc<128>(p.gc) : resident_gc<64>(p.gc));
   int ns = 1;
   if (max_pages > 1) {
     long long target = 8LL * resident;
-    ns = (int)((target + items - 1) / items);
+    ns = (int)((target + p.items - 1) / p.items);
     if (a.force_splits > 0) ns = a.force_splits;
     if (ns > max_pages) ns = max_pages;
     if (ns < 1) ns = 1;
   }
   a.split_pages = max_pages > 0 ? (max_pages + ns - 1) / ns : 1;
   a.n_splits = max_pages > 0 ? (max_pages + a.split_pages - 1) / a.split_pages : 1;
-  *n_items_out = items;
+  return p;
 }
 
 size_t decode_workspace_bytes(const DecodeArgs &a0, const DecodeBatch &batch) {
   DecodeArgs a = a0;
-  int items = 0;
-  plan(a, batch, &items);
+  plan(a, batch);
   if (a.n_splits <= 1) return 0;
   size_t rows = (size_t)a.n_caches * a.n_layers * a.n_q_heads;
   return rows * a.n_splits * (size_t)(a.head_dim + 2) * sizeof(float);
@@ -533,10 +510,7 @@ size_t decode_workspace_bytes(const DecodeArgs &a0, const DecodeBatch &batch) {
 int decode_launch(const DecodeArgs &a0, const DecodeBatch &batch, void *workspace,
                   size_t workspace_bytes, cudaStream_t s) {
   DecodeArgs a = a0;
-  int items = 0;
-  plan(a, batch, &items);
-  const int G = a.n_q_heads / a.geom.n_heads;
-  const int gc = pick_gc(G);
+  const Plan p = plan(a, batch);
   if (a.n_splits > 1) {
     size_t rows = (size_t)a.n_caches * a.n_layers * a.n_q_heads;
     size_t need = rows * a.n_splits * (size_t)(a.head_dim + 2) * sizeof(float);
@@ -548,10 +522,14 @@ int decode_launch(const DecodeArgs &a0, const DecodeBatch &batch, void *workspac
     a.part_m = a.part_o + rows * a.n_splits * a.head_dim;
     a.part_l = a.part_m + rows * a.n_splits;
   }
-  const int n_blocks = items * a.n_splits;
+  const int n_blocks = p.items * a.n_splits;
   if (n_blocks <= 0) return EAKV_OK;
-  int rc = a.head_dim == 128 ? dispatch_gc<128>(gc, a, batch, n_blocks, s)
-                             : dispatch_gc<64>(gc, a, batch, n_blocks, s);
+  int rc;
+  if (p.mma_gh)
+    rc = mma_launch(p.mma_gh, a, batch, n_blocks, s);
+  else
+    rc = a.head_dim == 128 ? dispatch_gc<128>(p.gc, a, batch, n_blocks, s)
+                           : dispatch_gc<64>(p.gc, a, batch, n_blocks, s);
   if (rc) return rc;
   if (a.n_splits > 1) {
     size_t rows = (size_t)a.n_caches * a.n_layers * a.n_q_heads;

@@ -1,0 +1,44 @@
+// decode_common.cuh - pieces shared by the fused decode kernels: the work
+// item decomposition (cache, layer, KV head, query-head group, split) and
+// small math helpers.
+#pragma once
+#include "internal.cuh"
+
+namespace eakv {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+struct Item {
+  int b, layer, lrow, h, hg, split;
+  int r0, r1;       // attended positions [r0, r1)
+  int pg0, npages;  // pages of this split
+};
+
+__device__ __forceinline__ Item decode_item(const DecodeArgs &a, const DecodeBatch &batch, int nhg) {
+  Item it;
+  int bid = blockIdx.x;
+  it.split = bid % a.n_splits; bid /= a.n_splits;
+  it.hg = bid % nhg; bid /= nhg;
+  it.h = bid % a.geom.n_heads; bid /= a.geom.n_heads;
+  it.lrow = bid % a.n_layers;
+  it.b = bid / a.n_layers;
+  it.layer = a.layer0 + it.lrow;
+  const int seq = batch.seq_len[it.b];
+  it.r0 = a.pos_begin > 0 ? a.pos_begin : 0;
+  it.r1 = a.pos_end < 0 ? seq : min(seq, a.pos_end);
+  int P0 = it.r0 / kPagePositions;
+  int P1 = it.r1 > it.r0 ? (it.r1 + kPagePositions - 1) / kPagePositions : P0;
+  it.pg0 = P0 + it.split * a.split_pages;
+  int pg1 = min(P1, it.pg0 + a.split_pages);
+  it.npages = pg1 > it.pg0 ? pg1 - it.pg0 : 0;
+  return it;
+}
+
+}  // namespace eakv

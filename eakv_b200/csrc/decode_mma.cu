@@ -1,0 +1,534 @@
+// decode_mma.cu - fused softmax attention over the Q4 cache on the tensor
+// cores (mma.sync m16n8k16, f16 operands, f32 accumulation), for GQA groups
+// of 4 or 8 query heads per KV head.
+//
+// Same work decomposition, page pipeline and merge as the CUDA-core kernel
+// in decode.cu; what changes is how the two contractions of a position
+// block are evaluated. Per warp and 16-position step:
+//
+//   S[(group, head, limb)][pos]  = Qlimbs[16 x 16 dims] * Knib[16 dims x 8 pos]   (x 8 k-steps)
+//   O[dims][(head, limb)]       += Vnib[16 dims x 16 pos] * P'[16 pos x (head, limb)]
+//
+// * The nibbles (0..15) are exact in f16. They are turned into f16 pairs in
+//   registers with one mask+or and one f16 subtract each: placing a nibble
+//   in the low mantissa bits of 1024.0 (0x6400) and subtracting 1024 gives
+//   it exactly; a high nibble is taken in place (bits 4..7), i.e. times 16,
+//   and the 1/16 is folded into the matching query element (K) or applied
+//   to the output row (V).
+// * The f32 operands (scaled queries; probabilities times V scale) are split
+//   into two f16 limbs, hi = f16(x) and lo = f16(x - hi), which carry ~22
+//   bits; the tensor core accumulates in f32. Queries are pre-scaled per
+//   head by a power of two, and P' per group by 2^-E with E the running max
+//   exponent of the V scales, so both stay inside the f16 range.
+// * Row r = limb*8 + u of the score tile: rows g and g+8 of a thread are the
+//   two limbs of the same (group, head), so a thread adds them in place.
+// * The dimension order inside a k-step is chosen so that a thread's two
+//   f16x2 B registers come from one 32-bit word of its position's nibble
+//   row; the query fragments are permuted the same way once per CTA.
+// * Scales and biases are applied in f32 outside the tensor core:
+//     score = s_k * dot + b_k * sum(q), O += (p s_v) n + p b_v.
+// * Online softmax in base 2 with a lazy maximum: the running max moves only
+//   when a block's max exceeds it by more than 8, so probabilities stay in
+//   [0, 256] and rescaling the accumulators is rare.
+#include <cuda_fp16.h>
+#include <math.h>
+
+#include "internal.cuh"
+#include "pipeline.cuh"
+#include "decode_common.cuh"
+
+namespace eakv {
+namespace {
+
+template <int HD, int GH>
+struct MCfg {
+  static constexpr int NG = HD / 64;                        // groups per position
+  static constexpr int KS = 4 * NG;                         // K k-steps of 16 dims
+  static constexpr int KMT = (GH == 8 && NG == 2) ? 2 : 1;  // score m-tiles (one per group)
+  static constexpr int VNT = GH == 8 ? 2 : 1;               // P' n-tiles (one per limb)
+  static constexpr int VMT = 4 * NG;                        // output m-tiles of 16 dims
+  static constexpr int NW = 4;                              // warps; each takes 16 positions of a page
+  static constexpr int THREADS = NW * 32;
+  static constexpr int NIB = kPagePositions * NG * 32;
+  static constexpr int PB = kPagePositions * NG * 40;
+  static constexpr int NSTAGE = HD == 128 ? 4 : 8;
+  static constexpr int STAGE_BYTES = 2 * PB;
+  static constexpr int RING = NSTAGE * STAGE_BYTES;
+  static constexpr int MERGE_BYTES = NW * GH * (HD + 2) * 4;
+  static constexpr int SMEM = (RING > MERGE_BYTES ? RING : MERGE_BYTES) + 2 * NSTAGE * 8;
+  static_assert(GH == 4 || GH == 8, "tensor-core path serves 4 or 8 query heads per KV head");
+};
+
+constexpr uint32_t kMagic = 0x64006400u;   // f16x2 (1024, 1024)
+
+__device__ __forceinline__ uint32_t f16x2_sub1024(uint32_t x) {
+  uint32_t r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(kMagic));
+  return r;
+}
+
+// f16x2 of the nibbles selected by `mask` (0x000F000F: low nibbles of bytes
+// 0 and 2, value n; 0x00F000F0: high nibbles, value 16 n).
+__device__ __forceinline__ uint32_t nib_pair(uint32_t w, uint32_t mask) {
+  return f16x2_sub1024((w & mask) | kMagic);
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// x = hi + lo in two f16 limbs: limb 0 = f16(x), limb 1 = f16(x - f16(x)).
+__device__ __forceinline__ void split2(float x0, float x1, uint32_t &h, uint32_t &l) {
+  __half2 hh = __floats2half2_rn(x0, x1);
+  float2 back = __half22float2(hh);
+  __half2 ll = __floats2half2_rn(x0 - back.x, x1 - back.y);
+  h = *reinterpret_cast<uint32_t *>(&hh);
+  l = *reinterpret_cast<uint32_t *>(&ll);
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Dimension (and its weight, 1 or 16) that K slot kk of k-step ks stands for.
+// Thread c of a position row holds bytes [8c, 8c+8) of each group as two
+// words; even k-steps use bytes 0/2 of a word, odd ones bytes 1/3; slots
+// 0..7 take low nibbles, 8..15 high nibbles (weight 16).
+__device__ __forceinline__ int kdim(int ks, int kk, int &weight) {
+  const int grp = ks >> 2, kl = ks & 3, m = kl >> 1, odd = kl & 1;
+  const int cc = (kk & 7) >> 1, e = kk & 1, second = kk >> 3;
+  const int byte = 8 * cc + 4 * m + odd + 2 * e;
+  weight = second ? 16 : 1;
+  return 64 * grp + byte + (second ? 32 : 0);
+}
+
+template <int HD, int GH>
+__global__ void __launch_bounds__(MCfg<HD, GH>::THREADS, 3)
+decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ DecodeBatch batch) {
+  using C = MCfg<HD, GH>;
+  constexpr int NG = C::NG;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (C::SMEM - 2 * C::NSTAGE * 8));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int G = a.n_q_heads / a.geom.n_heads;
+  const int nhg = G / GH;
+  const Item it = decode_item(a, batch, nhg);
+  const size_t kv_stride = (size_t)a.geom.n_heads * a.geom.n_pages;
+  const uint8_t *kpages = batch.base[it.b] + page_index(a.geom, it.layer, 0, it.h, 0) * C::PB;
+  const uint8_t *vpages = kpages + kv_stride * C::PB;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::NSTAGE; s++) {
+      mbar_init(smem_u32(&bars[s]), 1);
+      mbar_init(smem_u32(&bars[C::NSTAGE + s]), C::NW);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int i) {
+    const int st = i % C::NSTAGE;
+    const uint32_t full = smem_u32(&bars[st]);
+    mbar_arrive_expect_tx(full, 2 * C::PB);
+    const uint32_t dst = smem_u32(smem + st * C::STAGE_BYTES);
+    bulk_g2s(dst, kpages + (size_t)(it.pg0 + i) * C::PB, C::PB, full);
+    bulk_g2s(dst + C::PB, vpages + (size_t)(it.pg0 + i) * C::PB, C::PB, full);
+  };
+  if (threadIdx.x == 0)
+    for (int i = 0; i < it.npages && i < C::NSTAGE; i++) issue(i);
+
+  // ---- per-thread query fragments -----------------------------------------
+  // (group, head) of this thread's score rows, for each score m-tile
+  const int qh0 = it.h * G + it.hg * GH;
+  const float *qb = a.q + ((size_t)(it.b * a.n_layers + it.lrow) * a.n_q_heads + qh0) * HD;
+  auto row_pair = [&](int mt, int &grp_r, int &h_r) {
+    const int pi = (NG * GH >= 8) ? (mt * 8 + g) : (g % (NG * GH));
+    grp_r = pi / GH;
+    h_r = pi % GH;
+  };
+  int h_mine, grp_mine;
+  row_pair(0, grp_mine, h_mine);   // the head this thread scores (same for every m-tile)
+  // per-head power-of-two prescale keeping the query limbs inside f16
+  const float qscale = rsqrtf((float)HD) * kLog2e;
+  float hmax = 0.0f;
+  for (int d = 0; d < HD; d++) hmax = fmaxf(hmax, fabsf(qb[h_mine * HD + d] * qscale));
+  int qexp = 0;
+  frexpf(hmax > 0.0f ? hmax : 1.0f, &qexp);   // hmax in [2^(qexp-1), 2^qexp)
+  const float q_up = ldexpf(1.0f, 10 - qexp);     // largest |q| -> [512, 1024)
+  const float q_down = ldexpf(1.0f, qexp - 10);
+
+  uint32_t aq[C::KS][4];
+#pragma unroll
+  for (int ks = 0; ks < C::KS; ks++) {
+    const int mt = (C::KMT == 2) ? (ks >> 2) : 0;
+    int grp_r, h_r;
+    row_pair(mt, grp_r, h_r);
+    const bool live = grp_r == (ks >> 2);
+    float v[4];
+#pragma unroll
+    for (int s = 0; s < 4; s++) {   // slots 2c, 2c+1, 2c+8, 2c+9
+      const int kk = 2 * c + (s & 1) + (s >> 1) * 8;
+      int w;
+      const int d = kdim(ks, kk, w);
+      v[s] = live ? qb[h_r * HD + d] * qscale * q_up / (float)w : 0.0f;
+    }
+    uint32_t h01, l01, h23, l23;
+    split2(v[0], v[1], h01, l01);
+    split2(v[2], v[3], h23, l23);
+    aq[ks][0] = h01;   // row g   (limb 0), slots 2c, 2c+1
+    aq[ks][1] = l01;   // row g+8 (limb 1)
+    aq[ks][2] = h23;   // row g,   slots 2c+8, 2c+9
+    aq[ks][3] = l23;
+  }
+  // sum of the (unscaled by q_up) query over each group's dims, for the bias
+  float qsum[NG];
+#pragma unroll
+  for (int gg = 0; gg < NG; gg++) {
+    float s = 0.0f;
+    for (int d = 0; d < 64; d++) s += qb[h_mine * HD + 64 * gg + d] * qscale;
+    qsum[gg] = s;
+  }
+
+  // ---- accumulators -----------------------------------------------------------
+  float dv[C::VMT][C::VNT][4];
+#pragma unroll
+  for (int i = 0; i < C::VMT; i++)
+#pragma unroll
+    for (int n = 0; n < C::VNT; n++)
+#pragma unroll
+      for (int r = 0; r < 4; r++) dv[i][n][r] = 0.0f;
+  float m_run = -INFINITY, l_run = 0.0f;
+  float pb[NG];
+  int vexp[NG];   // running max biased exponent of the V scales, per group
+#pragma unroll
+  for (int gg = 0; gg < NG; gg++) {
+    pb[gg] = 0.0f;
+    vexp[gg] = -1;
+  }
+  // head of each P'/output column this thread holds: n = 2c + e
+  int hcol[2];
+#pragma unroll
+  for (int e = 0; e < 2; e++) hcol[e] = (C::VNT == 1) ? ((2 * c + e) % GH) : (2 * c + e);
+  const int my_limb = (C::VNT == 1) ? (g >> 2) : 0;
+
+  bool ok = true;
+  for (int i = 0; i < it.npages; i++) {
+    const int st = i % C::NSTAGE;
+    if (threadIdx.x == 0 && i >= 1 && i - 1 + C::NSTAGE < it.npages) {
+      const int pst = (i - 1) % C::NSTAGE;
+      if (!mbar_wait(smem_u32(&bars[C::NSTAGE + pst]), ((i - 1) / C::NSTAGE) & 1)) {
+        atomicOr(a.status, kStatusWaitTimeout);
+        ok = false;
+      } else {
+        issue(i - 1 + C::NSTAGE);
+      }
+    }
+    if (!ok || !mbar_wait(smem_u32(&bars[st]), (i / C::NSTAGE) & 1)) {
+      atomicOr(a.status, kStatusWaitTimeout);
+      ok = false;
+      break;
+    }
+    const uint8_t *ks_ = smem + st * C::STAGE_BYTES;
+    const uint8_t *vs_ = ks_ + C::PB;
+    const int p0 = 16 * warp;                         // first position of this warp's step
+    const int page_pos0 = (it.pg0 + i) * kPagePositions;
+
+    // positions of this thread's score/probability slots: 2c, 2c+1, 2c+8, 2c+9
+    int tpos[4];
+    bool tval[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      tpos[j] = p0 + 2 * c + (j & 1) + (j >> 1) * 8;
+      const int pos = page_pos0 + tpos[j];
+      tval[j] = pos >= it.r0 && pos < it.r1;
+    }
+
+    // ---- scores of the two 8-position tiles -------------------------------
+    float sc[4];
+#pragma unroll
+    for (int tile = 0; tile < 2; tile++) {
+      float dk[C::KMT][4];
+#pragma unroll
+      for (int mt = 0; mt < C::KMT; mt++)
+#pragma unroll
+        for (int r = 0; r < 4; r++) dk[mt][r] = 0.0f;
+      const uint8_t *row = ks_ + (p0 + 8 * tile + g) * (HD / 2) + 8 * c;
+#pragma unroll
+      for (int gg = 0; gg < NG; gg++) {
+        const uint2 wv = *reinterpret_cast<const uint2 *>(row + 32 * gg);
+#pragma unroll
+        for (int kl = 0; kl < 4; kl++) {
+          const int ks = 4 * gg + kl;
+          const uint32_t w = (kl >> 1) ? wv.y : wv.x;
+          const uint32_t y = (kl & 1) ? (w >> 8) : w;
+          const uint32_t b0 = nib_pair(y, 0x000F000Fu);
+          const uint32_t b1 = nib_pair(y, 0x00F000F0u);
+          const int mt = (C::KMT == 2) ? gg : 0;
+          mma16816(dk[mt], aq[ks][0], aq[ks][1], aq[ks][2], aq[ks][3], b0, b1);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        const int j = 2 * tile + e;
+        const float4 sbk = NG == 2
+            ? *reinterpret_cast<const float4 *>(ks_ + C::NIB + tpos[j] * NG * 8)
+            : make_float4(reinterpret_cast<const float2 *>(ks_ + C::NIB)[tpos[j]].x,
+                          reinterpret_cast<const float2 *>(ks_ + C::NIB)[tpos[j]].y, 0.f, 0.f);
+        float part = 0.0f;
+#pragma unroll
+        for (int mt = 0; mt < C::KMT; mt++) {
+          int grp_r, h_r;
+          row_pair(mt, grp_r, h_r);
+          const float dot = (dk[mt][e] + dk[mt][2 + e]) * q_down;
+          const float s = grp_r ? sbk.z : sbk.x, b = grp_r ? sbk.w : sbk.y;
+          part += fmaf(dot, s, b * qsum[grp_r]);
+        }
+        if (NG == 2 && C::KMT == 1) part += __shfl_xor_sync(0xffffffffu, part, 4 * GH);
+        sc[j] = tval[j] ? part : -INFINITY;
+      }
+    }
+
+    // ---- online softmax (base 2, lazy max) ----------------------------------
+    float tmax = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
+    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
+    const bool need = tmax > m_run + 8.0f;
+    if (__any_sync(0xffffffffu, need)) {
+      const float m_new = need ? tmax : m_run;
+      const float alpha = need ? ex2(m_run - m_new) : 1.0f;   // exp2(-inf) = 0
+      m_run = m_new;
+      l_run *= alpha;
+#pragma unroll
+      for (int gg = 0; gg < NG; gg++) pb[gg] *= alpha;
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        const float ac = __shfl_sync(0xffffffffu, alpha, 4 * hcol[e]);
+#pragma unroll
+        for (int mv = 0; mv < C::VMT; mv++)
+#pragma unroll
+          for (int n = 0; n < C::VNT; n++) {
+            dv[mv][n][e] *= ac;
+            dv[mv][n][2 + e] *= ac;
+          }
+      }
+    }
+    const float m_eff = m_run == -INFINITY ? 0.0f : m_run;
+    float p[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      p[j] = ex2(sc[j] - m_eff);
+      l_run += p[j];
+    }
+
+    // ---- P' fragments and the V contraction, group by group ------------------
+#pragma unroll
+    for (int gg = 0; gg < NG; gg++) {
+      float sv[4], bv[4];
+      int ex = 0;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float2 sb = reinterpret_cast<const float2 *>(vs_ + C::NIB)[tpos[j] * NG + gg];
+        sv[j] = tval[j] ? sb.x : 0.0f;
+        bv[j] = tval[j] ? sb.y : 0.0f;
+        ex = max(ex, (int)((__float_as_uint(sv[j]) >> 23) & 0xFF));
+      }
+      ex = max(ex, __shfl_xor_sync(0xffffffffu, ex, 1));
+      ex = max(ex, __shfl_xor_sync(0xffffffffu, ex, 2));
+      ex = min(max(ex, 1), 253);
+      if (ex > vexp[gg]) {   // warp-uniform: every lane holds the same positions
+        if (vexp[gg] >= 0) {
+          const int dd = ex - vexp[gg];
+          const float f = dd > 126 ? 0.0f : __uint_as_float((uint32_t)(127 - dd) << 23);
+#pragma unroll
+          for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int n = 0; n < C::VNT; n++)
+#pragma unroll
+              for (int r = 0; r < 4; r++) dv[4 * gg + j][n][r] *= f;
+        }
+        vexp[gg] = ex;
+      }
+      const float fs = __uint_as_float((uint32_t)(254 - vexp[gg]) << 23);   // 2^(127 - vexp)
+      float ps[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        ps[j] = p[j] * (sv[j] * fs);
+        pb[gg] = fmaf(p[j], bv[j], pb[gg]);
+      }
+      uint32_t bh0, bl0, bh1, bl1;   // limbs of positions (2c, 2c+1) and (2c+8, 2c+9)
+      split2(ps[0], ps[1], bh0, bl0);
+      split2(ps[2], ps[3], bh1, bl1);
+      uint32_t b0[C::VNT], b1[C::VNT];
+      if (C::VNT == 1) {
+        b0[0] = my_limb ? bl0 : bh0;
+        b1[0] = my_limb ? bl1 : bh1;
+      } else {
+        b0[0] = bh0;
+        b1[0] = bh1;
+        b0[C::VNT - 1] = bl0;
+        b1[C::VNT - 1] = bl1;
+      }
+      // V nibble words of this thread's four positions, byte 4g of the group
+      const uint8_t *vrow = vs_ + 32 * gg + 4 * g;
+      const uint32_t w0 = *reinterpret_cast<const uint32_t *>(vrow + tpos[0] * (HD / 2));
+      const uint32_t w1 = *reinterpret_cast<const uint32_t *>(vrow + tpos[1] * (HD / 2));
+      const uint32_t w2 = *reinterpret_cast<const uint32_t *>(vrow + tpos[2] * (HD / 2));
+      const uint32_t w3 = *reinterpret_cast<const uint32_t *>(vrow + tpos[3] * (HD / 2));
+      const uint32_t xa01 = __byte_perm(w0, w1, 0x5410), xa23 = __byte_perm(w0, w1, 0x7632);
+      const uint32_t xb01 = __byte_perm(w2, w3, 0x5410), xb23 = __byte_perm(w2, w3, 0x7632);
+#pragma unroll
+      for (int j = 0; j < 4; j++) {   // byte j of the word -> output m-tile 4*gg + j
+        const uint32_t xa = (j < 2) ? xa01 : xa23, xb = (j < 2) ? xb01 : xb23;
+        const uint32_t ya = (j & 1) ? (xa >> 8) : xa, yb = (j & 1) ? (xb >> 8) : xb;
+        const uint32_t a0 = nib_pair(ya, 0x000F000Fu);   // row g: low nibble, positions 2c, 2c+1
+        const uint32_t a1 = nib_pair(ya, 0x00F000F0u);   // row g+8: high nibble x16
+        const uint32_t a2 = nib_pair(yb, 0x000F000Fu);   // positions 2c+8, 2c+9
+        const uint32_t a3 = nib_pair(yb, 0x00F000F0u);
+#pragma unroll
+        for (int n = 0; n < C::VNT; n++) mma16816(dv[4 * gg + j][n], a0, a1, a2, a3, b0[n], b1[n]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&bars[C::NSTAGE + st]));
+  }
+  if (!__syncthreads_and(ok)) return;
+
+  // ---- per-warp totals --------------------------------------------------------
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+#pragma unroll
+  for (int gg = 0; gg < NG; gg++) {
+    pb[gg] += __shfl_xor_sync(0xffffffffu, pb[gg], 1);
+    pb[gg] += __shfl_xor_sync(0xffffffffu, pb[gg], 2);
+  }
+  // combine the two limbs of every output column
+#pragma unroll
+  for (int mv = 0; mv < C::VMT; mv++)
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      if (C::VNT == 1) dv[mv][0][r] += __shfl_xor_sync(0xffffffffu, dv[mv][0][r], 2);
+      else dv[mv][0][r] += dv[mv][C::VNT - 1][r];
+    }
+  float pbc[2][NG];   // bias accumulators of this thread's two column heads
+#pragma unroll
+  for (int e = 0; e < 2; e++)
+#pragma unroll
+    for (int gg = 0; gg < NG; gg++) pbc[e][gg] = __shfl_sync(0xffffffffu, pb[gg], 4 * hcol[e]);
+
+  __syncthreads();   // ring no longer read; reuse it for the merge
+  float *mw = reinterpret_cast<float *>(smem);   // [NW][GH]
+  float *lw = mw + C::NW * GH;                    // [NW][GH]
+  float *ow = lw + C::NW * GH;                    // [NW][GH][HD]
+  if (c == 0 && g < GH) {
+    // lane (g, 0) scores head g (g < GH rows carry every head once)
+    mw[warp * GH + h_mine] = m_run;
+    lw[warp * GH + h_mine] = l_run;
+  }
+  // after the limb sum, lanes c and c^2 hold the same columns (one limb pair)
+  const bool writer = (C::VNT == 1) ? (c < 2) : true;
+  if (writer) {
+#pragma unroll
+    for (int mv = 0; mv < C::VMT; mv++) {
+      const int gg = mv >> 2, j = mv & 3;
+      // undo the 2^(127 - vexp) applied to P': multiply by 2^(vexp - 127)
+      const float vs = __uint_as_float((uint32_t)(vexp[gg] < 0 ? 127 : vexp[gg]) << 23);
+      const int dlo = 64 * gg + 4 * g + j, dhi = dlo + 32;
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        const int h = hcol[e];
+        ow[(warp * GH + h) * HD + dlo] = fmaf(dv[mv][0][e], vs, pbc[e][gg]);
+        ow[(warp * GH + h) * HD + dhi] = fmaf(dv[mv][0][2 + e], vs * (1.0f / 16.0f), pbc[e][gg]);
+      }
+    }
+  }
+  __syncthreads();
+  const size_t row0 = (size_t)(it.b * a.n_layers + it.lrow) * a.n_q_heads + qh0;
+  for (int idx = threadIdx.x; idx < GH * HD; idx += C::THREADS) {
+    const int h = idx / HD, d = idx - h * HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < C::NW; w++) M = fmaxf(M, mw[w * GH + h]);
+    float O = 0.0f, L = 0.0f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < C::NW; w++) {
+        const float mwv = mw[w * GH + h];
+        const float f = mwv == -INFINITY ? 0.0f : ex2(mwv - M);
+        O = fmaf(f, ow[(w * GH + h) * HD + d], O);
+        L = fmaf(f, lw[w * GH + h], L);
+      }
+    }
+    const size_t row = row0 + h;
+    if (a.n_splits == 1) {
+      a.out[row * HD + d] = O / L;
+      if (a.lse && d == 0) a.lse[row] = L > 0.0f ? (M + log2f(L)) * kLn2 : -INFINITY;
+    } else {
+      const size_t pr = row * a.n_splits + it.split;
+      a.part_o[pr * HD + d] = O;
+      if (d == 0) {
+        a.part_m[pr] = M;
+        a.part_l[pr] = L;
+      }
+    }
+  }
+}
+
+template <int HD, int GH>
+int launch_one(const DecodeArgs &a, const DecodeBatch &b, int n_blocks, cudaStream_t s) {
+  using C = MCfg<HD, GH>;
+  auto fn = decode_mma_kernel<HD, GH>;
+  static unsigned long long attr_done = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_done >> (dev & 63) & 1)) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return check_cuda(e, "decode_mma: smem attribute");
+    attr_done |= 1ull << (dev & 63);
+  }
+  fn<<<n_blocks, C::THREADS, C::SMEM, s>>>(a, b);
+  return check_cuda(cudaGetLastError(), "decode_mma launch");
+}
+
+template <int HD, int GH>
+int resident_one() {
+  using C = MCfg<HD, GH>;
+  static int cached = 0;
+  if (cached) return cached;
+  cudaFuncSetAttribute(decode_mma_kernel<HD, GH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       C::SMEM);
+  int per_sm = 1, dev = 0, sms = 148;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_mma_kernel<HD, GH>, C::THREADS,
+                                                C::SMEM);
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cached = (per_sm < 1 ? 1 : per_sm) * sms;
+  return cached;
+}
+
+}  // namespace
+
+int mma_heads_per_cta(int G, int head_dim) {
+  if (head_dim != 64 && head_dim != 128) return 0;
+  if (G % 8 == 0) return 8;
+  if (G % 4 == 0) return 4;
+  return 0;
+}
+
+int mma_resident(int gh, int head_dim) {
+  if (head_dim == 128) return gh == 8 ? resident_one<128, 8>() : resident_one<128, 4>();
+  return gh == 8 ? resident_one<64, 8>() : resident_one<64, 4>();
+}
+
+int mma_launch(int gh, const DecodeArgs &a, const DecodeBatch &b, int n_blocks, cudaStream_t s) {
+  if (a.head_dim == 128)
+    return gh == 8 ? launch_one<128, 8>(a, b, n_blocks, s) : launch_one<128, 4>(a, b, n_blocks, s);
+  return gh == 8 ? launch_one<64, 8>(a, b, n_blocks, s) : launch_one<64, 4>(a, b, n_blocks, s);
+}
+
+}  // namespace eakv

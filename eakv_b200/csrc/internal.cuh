@@ -123,6 +123,7 @@ struct DecodeArgs {
   float *lse;                       // optional [cache][layer][q_head] natural-log LSE
   int *status;                      // device status word (bounded waits)
   int force_splits;                 // > 0: use this many splits (tests)
+  int force_path;                   // 1: CUDA-core kernel even where tensor cores apply
   // filled by the planner
   int n_splits, split_pages;
   float *part_m, *part_l, *part_o;
@@ -133,6 +134,11 @@ size_t decode_workspace_bytes(const DecodeArgs &a, const DecodeBatch &batch);
 int lse_combine_launch(int n_parts, int n_rows, int head_dim, const float *parts,
                        const float *lse, float *out, float *lse_out, cudaStream_t s);
 int *device_status_ptr();   // status word of the current device
+// decode_mma.cu: tensor-core decode for 4 or 8 query heads per KV head
+int mma_heads_per_cta(int G, int head_dim);   // 0 when the shape is not served
+int mma_resident(int gh, int head_dim);
+int mma_launch(int gh, const DecodeArgs &a, const DecodeBatch &b, int n_blocks, cudaStream_t s);
+extern thread_local int t_force_path;
 extern thread_local int t_force_splits;
 
 }  // namespace eakv

@@ -25,9 +25,15 @@ namespace {
 
 constexpr int kThreads = 256;
 
+// The reference truncates with x86 cvttss2si, which returns INT_MIN for NaN
+// and for anything outside the int32 range; the clamp then gives 0. That
+// case is real: a group whose range is denormal has inv = 15/range = +inf,
+// so every element above the minimum maps to +inf (and the minimum to NaN).
+// The device conversion would saturate +inf to INT_MAX (-> 15), so those
+// inputs are sent to 0 explicitly.
 __device__ __forceinline__ int quant_one(float x, float mn, float inv) {
   float t = __fadd_rn(__fmul_rn(__fsub_rn(x, mn), inv), 0.5f);
-  int q = __float2int_rz(t);   // NaN -> 0; the reference's INT_MIN clamps to 0 too
+  int q = (t < 2147483648.0f) ? __float2int_rz(t) : 0;   // NaN compares false
   return q < 0 ? 0 : (q > 15 ? 15 : q);
 }
 

@@ -133,6 +133,12 @@ int eakv_lse_combine(int n_parts, int n_rows, int head_dim,
  * can exercise the split + combine path on small caches. */
 int eakv_test_force_splits(int n);
 
+/* path 1 makes later fused / decode calls on this host thread use the
+ * CUDA-core kernel even for shapes the tensor-core kernel serves (GQA
+ * groups of 4 or 8); 0 restores the automatic choice. For tests and
+ * side-by-side measurements. */
+int eakv_test_force_path(int path);
+
 #ifdef __cplusplus
 }
 #endif

@@ -15,8 +15,15 @@ pytestmark = pytest.mark.gpu
 @pytest.fixture(autouse=True)
 def _reset_splits():
     E.force_splits(0)
+    E.force_path(0)
     yield
     E.force_splits(0)
+    E.force_path(0)
+
+
+# "auto" runs the tensor-core kernel for 4 or 8 query heads per KV head and
+# the CUDA-core kernel otherwise; "simt" forces the CUDA-core kernel
+PATHS = ["auto", "simt"]
 
 
 @pytest.mark.parametrize("name", ["mha128", "gqa64_8to2", "gqa128_4to1", "mha64"])
@@ -43,8 +50,10 @@ CASES = [
 ]
 
 
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("L,nq,nkv,hd,S,maxS", CASES)
-def test_fused_random(gpu, L, nq, nkv, hd, S, maxS):
+def test_fused_random(gpu, L, nq, nkv, hd, S, maxS, path):
+    E.force_path(1 if path == "simt" else 0)
     rng = np.random.default_rng(S * 7 + nq)
     data = kv_data(rng, L, nkv, S, hd)
     rc = O.RefCache(L, nkv, hd, maxS)
@@ -56,9 +65,11 @@ def test_fused_random(gpu, L, nq, nkv, hd, S, maxS):
             assert_close(c.fused(q, l, nq, nkv), rc.fused(q, l, nq, nkv), what=f"layer {l}")
 
 
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("splits", [1, 2, 3, 7, 64])
-def test_forced_splits(gpu, splits):
+def test_forced_splits(gpu, splits, path):
     """Split + exact LSE combine gives the same result as one pass."""
+    E.force_path(1 if path == "simt" else 0)
     L, nq, nkv, hd, S = 1, 16, 4, 128, 1111
     rng = np.random.default_rng(splits)
     data = kv_data(rng, L, nkv, S, hd)
@@ -71,8 +82,10 @@ def test_forced_splits(gpu, splits):
         assert_close(c.fused(q, 0, nq, nkv), rc.fused(q, 0, nq, nkv), what=f"{splits} splits")
 
 
-def test_large_scores_softmax_stability(gpu):
+@pytest.mark.parametrize("path", PATHS)
+def test_large_scores_softmax_stability(gpu, path):
     """Queries scaled x30: scores in the hundreds, softmax near one-hot."""
+    E.force_path(1 if path == "simt" else 0)
     L, nq, nkv, hd, S = 1, 8, 2, 128, 500
     rng = np.random.default_rng(77)
     data = kv_data(rng, L, nkv, S, hd)
@@ -179,3 +192,35 @@ def test_restore_limits_attention(gpu):
 
 def test_device_status_clean(gpu):
     assert E.device_status(0, reset=False) == 0
+
+
+@pytest.mark.parametrize("vscale", [1e-30, 1e-3, 1.0, 1e4, 1e30])
+def test_extreme_value_scales(gpu, vscale):
+    """V values over 60 orders of magnitude and a K/V range that grows
+    along the sequence: the tensor-core path rescales its f16 operands."""
+    L, nq, nkv, hd, S = 1, 16, 4, 128, 640
+    rng = np.random.default_rng(int(np.log10(vscale)) + 100)
+    data = kv_data(rng, L, nkv, S, hd)
+    data[0, 1] *= np.float32(vscale)
+    data[0, 1, :, S // 2:] *= np.float32(64.0)      # scales jump mid-sequence
+    rc = O.RefCache(L, nkv, hd, S)
+    rc.load_raw(data, S)
+    q = rng.standard_normal(nq * hd).astype(np.float32)
+    with E.Cache(L, nkv, hd, S) as c:
+        assert c.load_raw(data, S) == 0
+        ref = rc.fused(q, 0, nq, nkv)
+        got = c.fused(q, 0, nq, nkv)
+        assert_close(got / vscale, ref / vscale, what=f"V scale {vscale}")
+
+
+@pytest.mark.parametrize("qscale", [1e-6, 1e-2, 1e3])
+def test_query_magnitudes(gpu, qscale):
+    L, nq, nkv, hd, S = 1, 32, 4, 64, 300
+    rng = np.random.default_rng(5)
+    data = kv_data(rng, L, nkv, S, hd)
+    rc = O.RefCache(L, nkv, hd, S)
+    rc.load_raw(data, S)
+    q = (rng.standard_normal(nq * hd) * qscale).astype(np.float32)
+    with E.Cache(L, nkv, hd, S) as c:
+        assert c.load_raw(data, S) == 0
+        assert_close(c.fused(q, 0, nq, nkv), rc.fused(q, 0, nq, nkv), what=f"q x{qscale}")
