@@ -111,15 +111,15 @@ decode_simt_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::NSTAGE; s++) {
-      mbar_init(smem_u32(&bars[s]), 1);                               // full
-      mbar_init(smem_u32(&bars[C::NSTAGE + s]), C::NW);      // empty
+      mbar_init(smem_u32(&bars[s]), 1);                               // stage filled
+      reinterpret_cast<int *>(&bars[C::NSTAGE])[s] = 0;               // release count
     }
     fence_mbar_init();
   }
   __syncthreads();
 
-  // Thread 0 also runs the copy engine: it fills the first NSTAGE stages
-  // here and refills a stage once every warp has released it.
+  // Thread 0 fills the first NSTAGE stages; afterwards the last warp to
+  // release a stage refills it (no thread ever waits for a stage to drain).
   auto issue = [&](int i) {
     const int st = i % C::NSTAGE;
     const uint32_t full = smem_u32(&bars[st]);
@@ -175,16 +175,6 @@ decode_simt_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
   bool ok = true;
   for (int i = 0; i < it.npages; i++) {
     const int st = i % C::NSTAGE;
-    if (threadIdx.x == 0 && i >= 1 && i - 1 + C::NSTAGE < it.npages) {
-      // stage of page i-1: wait until all warps released it, then refill
-      const int pst = (i - 1) % C::NSTAGE;
-      if (!mbar_wait(smem_u32(&bars[C::NSTAGE + pst]), ((i - 1) / C::NSTAGE) & 1)) {
-        atomicOr(a.status, kStatusWaitTimeout);
-        ok = false;
-      } else {
-        issue(i - 1 + C::NSTAGE);
-      }
-    }
     if (!ok || !mbar_wait(smem_u32(&bars[st]), (i / C::NSTAGE) & 1)) {
       atomicOr(a.status, kStatusWaitTimeout);
       ok = false;
@@ -279,7 +269,10 @@ decode_simt_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(smem_u32(&bars[C::NSTAGE + st]));
+    // the last warp to finish with this stage refills it with page i+NSTAGE
+    if (lane == 0 && stage_release_last(reinterpret_cast<int *>(&bars[C::NSTAGE]) + st, C::NW) &&
+        i + C::NSTAGE < it.npages)
+      issue(i + C::NSTAGE);
   }
   // every wait above is bounded, so all threads get here; leave together
   if (!__syncthreads_and(ok)) return;

@@ -33,6 +33,8 @@
 #include <cuda_fp16.h>
 #include <math.h>
 
+#include <type_traits>
+
 #include "internal.cuh"
 #include "pipeline.cuh"
 #include "decode_common.cuh"
@@ -55,7 +57,10 @@ struct MCfg {
   static constexpr int STAGE_BYTES = 2 * PB;
   static constexpr int RING = NSTAGE * STAGE_BYTES;
   static constexpr int MERGE_BYTES = NW * GH * (HD + 2) * 4;
-  static constexpr int SMEM = (RING > MERGE_BYTES ? RING : MERGE_BYTES) + 2 * NSTAGE * 8;
+  static constexpr int MAIN = (RING > MERGE_BYTES ? RING : MERGE_BYTES);
+  static constexpr int QOFF = MAIN + 2 * NSTAGE * 8;          // scaled queries [GH][HD]
+  static constexpr int STATOFF = QOFF + GH * HD * 4;           // [GH] max|q|, [GH][NG] sums
+  static constexpr int SMEM = STATOFF + GH * (1 + NG) * 4;
   static_assert(GH == 4 || GH == 8, "tensor-core path serves 4 or 8 query heads per KV head");
 };
 
@@ -67,10 +72,18 @@ __device__ __forceinline__ uint32_t f16x2_sub1024(uint32_t x) {
   return r;
 }
 
+// (w & mask) | magic as one three-input logic op; written out because the
+// compiler otherwise splits it in two when both constants are immediates.
+__device__ __forceinline__ uint32_t and_or(uint32_t w, uint32_t mask, uint32_t magic) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(w), "r"(mask), "r"(magic));
+  return r;
+}
+
 // f16x2 of the nibbles selected by `mask` (0x000F000F: low nibbles of bytes
 // 0 and 2, value n; 0x00F000F0: high nibbles, value 16 n).
 __device__ __forceinline__ uint32_t nib_pair(uint32_t w, uint32_t mask) {
-  return f16x2_sub1024((w & mask) | kMagic);
+  return f16x2_sub1024(and_or(w, mask, kMagic));
 }
 
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
@@ -109,12 +122,14 @@ __device__ __forceinline__ int kdim(int ks, int kk, int &weight) {
 }
 
 template <int HD, int GH>
-__global__ void __launch_bounds__(MCfg<HD, GH>::THREADS, 3)
+__global__ void __launch_bounds__(MCfg<HD, GH>::THREADS, 4)
 decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ DecodeBatch batch) {
   using C = MCfg<HD, GH>;
   constexpr int NG = C::NG;
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (C::SMEM - 2 * C::NSTAGE * 8));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::MAIN);
+  float *q_s = reinterpret_cast<float *>(smem + C::QOFF);
+  float *stat_s = reinterpret_cast<float *>(smem + C::STATOFF);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const int G = a.n_q_heads / a.geom.n_heads;
@@ -126,8 +141,8 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::NSTAGE; s++) {
-      mbar_init(smem_u32(&bars[s]), 1);
-      mbar_init(smem_u32(&bars[C::NSTAGE + s]), C::NW);
+      mbar_init(smem_u32(&bars[s]), 1);                               // stage filled
+      reinterpret_cast<int *>(&bars[C::NSTAGE])[s] = 0;               // release count
     }
     fence_mbar_init();
   }
@@ -154,10 +169,28 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
   };
   int h_mine, grp_mine;
   row_pair(0, grp_mine, h_mine);   // the head this thread scores (same for every m-tile)
-  // per-head power-of-two prescale keeping the query limbs inside f16
   const float qscale = rsqrtf((float)HD) * kLog2e;
-  float hmax = 0.0f;
-  for (int d = 0; d < HD; d++) hmax = fmaxf(hmax, fabsf(qb[h_mine * HD + d] * qscale));
+  // stage the scaled query block; one warp per head computes max|q| and
+  // the per-group sums (for the bias term)
+  for (int i = threadIdx.x; i < GH * HD; i += C::THREADS) q_s[i] = qb[i] * qscale;
+  __syncthreads();
+  for (int h = warp; h < GH; h += C::NW) {
+    float mx = 0.0f;
+    for (int d = lane; d < HD; d += 32) mx = fmaxf(mx, fabsf(q_s[h * HD + d]));
+#pragma unroll
+    for (int gg = 0; gg < NG; gg++) {
+      float sm = q_s[h * HD + 64 * gg + lane] + q_s[h * HD + 64 * gg + 32 + lane];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+      if (lane == 0) stat_s[GH + h * NG + gg] = sm;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) stat_s[h] = mx;
+  }
+  __syncthreads();
+  // per-head power-of-two prescale keeping the query limbs inside f16
+  const float hmax = stat_s[h_mine];
   int qexp = 0;
   frexpf(hmax > 0.0f ? hmax : 1.0f, &qexp);   // hmax in [2^(qexp-1), 2^qexp)
   const float q_up = ldexpf(1.0f, 10 - qexp);     // largest |q| -> [512, 1024)
@@ -176,7 +209,7 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
       const int kk = 2 * c + (s & 1) + (s >> 1) * 8;
       int w;
       const int d = kdim(ks, kk, w);
-      v[s] = live ? qb[h_r * HD + d] * qscale * q_up / (float)w : 0.0f;
+      v[s] = live ? q_s[h_r * HD + d] * (q_up / (float)w) : 0.0f;
     }
     uint32_t h01, l01, h23, l23;
     split2(v[0], v[1], h01, l01);
@@ -189,11 +222,7 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
   // sum of the (unscaled by q_up) query over each group's dims, for the bias
   float qsum[NG];
 #pragma unroll
-  for (int gg = 0; gg < NG; gg++) {
-    float s = 0.0f;
-    for (int d = 0; d < 64; d++) s += qb[h_mine * HD + 64 * gg + d] * qscale;
-    qsum[gg] = s;
-  }
+  for (int gg = 0; gg < NG; gg++) qsum[gg] = stat_s[GH + h_mine * NG + gg];
 
   // ---- accumulators -----------------------------------------------------------
   float dv[C::VMT][C::VNT][4];
@@ -217,27 +246,12 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
   for (int e = 0; e < 2; e++) hcol[e] = (C::VNT == 1) ? ((2 * c + e) % GH) : (2 * c + e);
   const int my_limb = (C::VNT == 1) ? (g >> 2) : 0;
 
-  bool ok = true;
-  for (int i = 0; i < it.npages; i++) {
-    const int st = i % C::NSTAGE;
-    if (threadIdx.x == 0 && i >= 1 && i - 1 + C::NSTAGE < it.npages) {
-      const int pst = (i - 1) % C::NSTAGE;
-      if (!mbar_wait(smem_u32(&bars[C::NSTAGE + pst]), ((i - 1) / C::NSTAGE) & 1)) {
-        atomicOr(a.status, kStatusWaitTimeout);
-        ok = false;
-      } else {
-        issue(i - 1 + C::NSTAGE);
-      }
-    }
-    if (!ok || !mbar_wait(smem_u32(&bars[st]), (i / C::NSTAGE) & 1)) {
-      atomicOr(a.status, kStatusWaitTimeout);
-      ok = false;
-      break;
-    }
-    const uint8_t *ks_ = smem + st * C::STAGE_BYTES;
+  // One 16-position step of a staged page (this warp's quarter of it).
+  // FULL: every position of the page is attended (no per-position masks).
+  auto page_body = [&](auto full_tag, const uint8_t *ks_, int page_pos0) {
+    constexpr bool FULL = decltype(full_tag)::value;
     const uint8_t *vs_ = ks_ + C::PB;
     const int p0 = 16 * warp;                         // first position of this warp's step
-    const int page_pos0 = (it.pg0 + i) * kPagePositions;
 
     // positions of this thread's score/probability slots: 2c, 2c+1, 2c+8, 2c+9
     int tpos[4];
@@ -246,7 +260,27 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
     for (int j = 0; j < 4; j++) {
       tpos[j] = p0 + 2 * c + (j & 1) + (j >> 1) * 8;
       const int pos = page_pos0 + tpos[j];
-      tval[j] = pos >= it.r0 && pos < it.r1;
+      tval[j] = FULL || (pos >= it.r0 && pos < it.r1);
+    }
+    // (scale, bias) of K and V for the four positions, every group
+    float sk[4][NG], bk[4][NG], sv[4][NG], bv[4][NG];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      if (NG == 2) {
+        const float4 k4 = *reinterpret_cast<const float4 *>(ks_ + C::NIB + tpos[j] * 16);
+        const float4 v4 = *reinterpret_cast<const float4 *>(vs_ + C::NIB + tpos[j] * 16);
+        sk[j][0] = k4.x; bk[j][0] = k4.y; sk[j][NG - 1] = k4.z; bk[j][NG - 1] = k4.w;
+        sv[j][0] = v4.x; bv[j][0] = v4.y; sv[j][NG - 1] = v4.z; bv[j][NG - 1] = v4.w;
+      } else {
+        const float2 k2 = *reinterpret_cast<const float2 *>(ks_ + C::NIB + tpos[j] * 8);
+        const float2 v2 = *reinterpret_cast<const float2 *>(vs_ + C::NIB + tpos[j] * 8);
+        sk[j][0] = k2.x; bk[j][0] = k2.y;
+        sv[j][0] = v2.x; bv[j][0] = v2.y;
+      }
+      if (!FULL && !tval[j]) {
+#pragma unroll
+        for (int gg = 0; gg < NG; gg++) sv[j][gg] = bv[j][gg] = 0.0f;
+      }
     }
 
     // ---- scores of the two 8-position tiles -------------------------------
@@ -276,21 +310,18 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
 #pragma unroll
       for (int e = 0; e < 2; e++) {
         const int j = 2 * tile + e;
-        const float4 sbk = NG == 2
-            ? *reinterpret_cast<const float4 *>(ks_ + C::NIB + tpos[j] * NG * 8)
-            : make_float4(reinterpret_cast<const float2 *>(ks_ + C::NIB)[tpos[j]].x,
-                          reinterpret_cast<const float2 *>(ks_ + C::NIB)[tpos[j]].y, 0.f, 0.f);
         float part = 0.0f;
 #pragma unroll
         for (int mt = 0; mt < C::KMT; mt++) {
           int grp_r, h_r;
           row_pair(mt, grp_r, h_r);
           const float dot = (dk[mt][e] + dk[mt][2 + e]) * q_down;
-          const float s = grp_r ? sbk.z : sbk.x, b = grp_r ? sbk.w : sbk.y;
-          part += fmaf(dot, s, b * qsum[grp_r]);
+          const float s_ = (NG == 2 && grp_r) ? sk[j][NG - 1] : sk[j][0];
+          const float b_ = (NG == 2 && grp_r) ? bk[j][NG - 1] : bk[j][0];
+          part += fmaf(dot, s_, b_ * ((NG == 2 && grp_r) ? qsum[NG - 1] : qsum[0]));
         }
         if (NG == 2 && C::KMT == 1) part += __shfl_xor_sync(0xffffffffu, part, 4 * GH);
-        sc[j] = tval[j] ? part : -INFINITY;
+        sc[j] = (FULL || tval[j]) ? part : -INFINITY;
       }
     }
 
@@ -329,18 +360,11 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
     // ---- P' fragments and the V contraction, group by group ------------------
 #pragma unroll
     for (int gg = 0; gg < NG; gg++) {
-      float sv[4], bv[4];
-      int ex = 0;
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const float2 sb = reinterpret_cast<const float2 *>(vs_ + C::NIB)[tpos[j] * NG + gg];
-        sv[j] = tval[j] ? sb.x : 0.0f;
-        bv[j] = tval[j] ? sb.y : 0.0f;
-        ex = max(ex, (int)((__float_as_uint(sv[j]) >> 23) & 0xFF));
-      }
-      ex = max(ex, __shfl_xor_sync(0xffffffffu, ex, 1));
-      ex = max(ex, __shfl_xor_sync(0xffffffffu, ex, 2));
-      ex = min(max(ex, 1), 253);
+      // largest V scale of the step (scales are >= 0: compare as floats)
+      float smax = fmaxf(fmaxf(sv[0][gg], sv[1][gg]), fmaxf(sv[2][gg], sv[3][gg]));
+      smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, 1));
+      smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, 2));
+      const int ex = min(max((int)(__float_as_uint(smax) >> 23) & 0xFF, 1), 253);
       if (ex > vexp[gg]) {   // warp-uniform: every lane holds the same positions
         if (vexp[gg] >= 0) {
           const int dd = ex - vexp[gg];
@@ -358,8 +382,8 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
       float ps[4];
 #pragma unroll
       for (int j = 0; j < 4; j++) {
-        ps[j] = p[j] * (sv[j] * fs);
-        pb[gg] = fmaf(p[j], bv[j], pb[gg]);
+        ps[j] = p[j] * (sv[j][gg] * fs);
+        pb[gg] = fmaf(p[j], bv[j][gg], pb[gg]);
       }
       uint32_t bh0, bl0, bh1, bl1;   // limbs of positions (2c, 2c+1) and (2c+8, 2c+9)
       split2(ps[0], ps[1], bh0, bl0);
@@ -394,8 +418,28 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
         for (int n = 0; n < C::VNT; n++) mma16816(dv[4 * gg + j][n], a0, a1, a2, a3, b0[n], b1[n]);
       }
     }
+  };
+
+  bool ok = true;
+  for (int i = 0; i < it.npages; i++) {
+    const int st = i % C::NSTAGE;
+    if (!ok || !mbar_wait(smem_u32(&bars[st]), (i / C::NSTAGE) & 1)) {
+      atomicOr(a.status, kStatusWaitTimeout);
+      ok = false;
+      break;
+    }
+    const uint8_t *ks_ = smem + st * C::STAGE_BYTES;
+    const int page_pos0 = (it.pg0 + i) * kPagePositions;
+    const bool full = page_pos0 >= it.r0 && page_pos0 + kPagePositions <= it.r1;
+    if (full)
+      page_body(std::true_type{}, ks_, page_pos0);
+    else
+      page_body(std::false_type{}, ks_, page_pos0);
     __syncwarp();
-    if (lane == 0) mbar_arrive(smem_u32(&bars[C::NSTAGE + st]));
+    // the last warp to finish with this stage refills it with page i+NSTAGE
+    if (lane == 0 && stage_release_last(reinterpret_cast<int *>(&bars[C::NSTAGE]) + st, C::NW) &&
+        i + C::NSTAGE < it.npages)
+      issue(i + C::NSTAGE);
   }
   if (!__syncthreads_and(ok)) return;
 

@@ -63,6 +63,25 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t
       : "memory");
 }
 
+// Orders this thread's earlier generic-proxy shared-memory accesses before
+// its later async-proxy (bulk copy) accesses to the same memory.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Stage release without waiting: every consumer warp calls this (lane 0)
+// after its last read of a stage; the call that completes the set returns
+// true exactly once, resets the counter, and its caller refills the stage.
+__device__ __forceinline__ bool stage_release_last(int *counter, int n_warps) {
+  __threadfence_block();                       // this warp's reads happen-before
+  const int old = atomicAdd(counter, 1);
+  if (old != n_warps - 1) return false;
+  *counter = 0;
+  __threadfence_block();                       // the other warps' reads are visible
+  fence_proxy_async_smem();                    // ... and ordered before the copy
+  return true;
+}
+
 // Named barrier over `count` threads (a multiple of 32).
 __device__ __forceinline__ void named_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
