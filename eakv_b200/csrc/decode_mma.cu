@@ -51,6 +51,8 @@ struct MCfg {
   static constexpr int VMT = 4 * NG;                        // output m-tiles of 16 dims
   static constexpr int NW = 4;                              // warps; each takes 16 positions of a page
   static constexpr int THREADS = NW * 32;
+  // CTAs per SM the register budget is cut for (128 registers at 4)
+  static constexpr int MINB = (HD == 128 && GH == 8) ? 3 : 4;
   static constexpr int NIB = kPagePositions * NG * 32;
   static constexpr int PB = kPagePositions * NG * 40;
   static constexpr int NSTAGE = HD == 128 ? 4 : 8;
@@ -122,7 +124,7 @@ __device__ __forceinline__ int kdim(int ks, int kk, int &weight) {
 }
 
 template <int HD, int GH>
-__global__ void __launch_bounds__(MCfg<HD, GH>::THREADS, 4)
+__global__ void __launch_bounds__(MCfg<HD, GH>::THREADS, MCfg<HD, GH>::MINB)
 decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ DecodeBatch batch) {
   using C = MCfg<HD, GH>;
   constexpr int NG = C::NG;

@@ -72,13 +72,14 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 // Stage release without waiting: every consumer warp calls this (lane 0)
 // after its last read of a stage; the call that completes the set returns
 // true exactly once, resets the counter, and its caller refills the stage.
+// Every value a warp loaded from the stage has been consumed by the time it
+// releases it, so those reads are complete; the counter itself is updated
+// atomically. The proxy fence orders them before the refill's async write.
 __device__ __forceinline__ bool stage_release_last(int *counter, int n_warps) {
-  __threadfence_block();                       // this warp's reads happen-before
   const int old = atomicAdd(counter, 1);
   if (old != n_warps - 1) return false;
   *counter = 0;
-  __threadfence_block();                       // the other warps' reads are visible
-  fence_proxy_async_smem();                    // ... and ordered before the copy
+  fence_proxy_async_smem();
   return true;
 }
 
