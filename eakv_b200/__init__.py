@@ -72,6 +72,7 @@ SIGNATURES = {
     "eakv_attention_fused_device": (_I, [_P, _P, _I, _I, _I, _P]),
     "eakv_decode_attention": (_I, [_P, _I, _P, _I, _P, _P]),
     "eakv_decode_attention_host": (_I, [_P, _I, _P, _I, _P, _P]),
+    "eakv_decode_attention_noalloc": (_I, [_P, _I, _P, _I, _P, _P]),
     "eakv_decode_launches": (_I, [_P, _I, _I]),
     "eakv_decode_attention_partial": (_I, [_P, _I, _P, _I, _I, _I, _P, _P, _P]),
     "eakv_lse_combine": (_I, [_I, _I, _I, _P, _P, _P, _P, _P]),
@@ -275,6 +276,14 @@ def decode_attention(caches, d_queries, n_q_heads, d_output, stream=None):
     return _check(lib().eakv_decode_attention(arr, len(caches), _ptr(d_queries), n_q_heads,
                                               _ptr(d_output), stream),
                   "eakv_decode_attention")
+
+
+def decode_attention_noalloc(caches, d_queries, n_q_heads, d_output, stream=None):
+    """eakv_decode_attention without any device allocation (fixed 4 MiB
+    workspace in the library; see eakv_cuda.h). Returns the C return code."""
+    arr = _handles(caches)
+    return lib().eakv_decode_attention_noalloc(arr, len(caches), _ptr(d_queries), n_q_heads,
+                                               _ptr(d_output), stream)
 
 
 def decode_attention_host(caches, queries, n_q_heads, output, stream=None):

@@ -97,6 +97,19 @@ int eakv_attention_fused_device(const eakv_cache_t *cache,
 int eakv_decode_attention(const eakv_cache_t *const *caches, int n_caches,
                           const float *d_queries, int n_q_heads,
                           float *d_output, void *stream);
+/* Same as eakv_decode_attention, for callers that cannot allocate device
+ * memory: no counterpart in the reference, whose CPU path has no device
+ * memory at all. A framework whose caching allocator owns the GPU, or a
+ * decode loop that must not block on cudaMalloc/cudaFree, gets the
+ * split-merge workspace from a fixed 4 MiB array in the library's device
+ * image (held by every GPU that loads the library) instead of from cache
+ * scratch grown with cudaMalloc. Calls needing more than 4 MiB of workspace
+ * return EAKV_ERR_INVALID. All calls on a device share the array: calls
+ * whose kernels overlap on the GPU race. The first call on a device looks
+ * up the array's address and should come before any stream capture. */
+int eakv_decode_attention_noalloc(const eakv_cache_t *const *caches,
+                                  int n_caches, const float *d_queries,
+                                  int n_q_heads, float *d_output, void *stream);
 /* Same with host buffers; copies in, decodes, copies out, synchronizes. */
 int eakv_decode_attention_host(const eakv_cache_t *const *caches,
                                int n_caches, const float *queries,
