@@ -302,6 +302,8 @@ def run_b200(args, cfg, world, rank, local):
     E.set_device(local)
     if args.force_simt:
         E.force_path(1)
+    if args.splits:
+        E.force_splits(args.splits)
     dev = torch.device("cuda", local)
     caches = build_caches(E, torch, cfg, dev, seed=1234 + rank)
     B, L, nq, hd = cfg["B"], cfg["L"], cfg["nq"], cfg["hd"]
@@ -428,6 +430,8 @@ def main():
     ap.add_argument("--seq", type=int, default=0, help="override cached positions")
     ap.add_argument("--force-simt", action="store_true",
                     help="time the CUDA-core decode kernel even where tensor cores apply")
+    ap.add_argument("--splits", type=int, default=0,
+                    help="force this many sequence splits per row (0: planner's choice)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
