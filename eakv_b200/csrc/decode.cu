@@ -382,6 +382,7 @@ __global__ void lse_combine_kernel(int n_parts, size_t n_rows, int HD, const flo
   if (M != -INFINITY) {
     for (int p = 0; p < n_parts; p++) {
       const float lp = lse[p * n_rows + row];
+      if (lp == -INFINITY) continue;   // empty range: its output is 0/0
       const float f = ex2((lp - M) * kLog2e);
       if (d < HD) O = fmaf(f, parts[(p * n_rows + row) * HD + d], O);
       L += f;

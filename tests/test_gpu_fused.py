@@ -140,7 +140,7 @@ def test_partial_ranges_and_lse_combine(gpu):
     rc = O.RefCache(L, nkv, hd, S)
     rc.load_raw(data, S)
     q = rng.standard_normal((1, L, nq, hd)).astype(np.float32)
-    bounds = [0, 100, 101, 640, 1000]
+    bounds = [0, 100, 100, 101, 640, 1000]   # includes an empty range
     P = len(bounds) - 1
     with E.Cache(L, nkv, hd, S) as c:
         assert c.load_raw(data, S) == 0
@@ -151,6 +151,9 @@ def test_partial_ranges_and_lse_combine(gpu):
             E.decode_attention_partial([c], dq, nq, bounds[p], bounds[p + 1], parts[p], lse[p])
         c.synchronize()
         for p in range(P):
+            if bounds[p] == bounds[p + 1]:
+                assert torch.isneginf(lse[p]).all()   # empty range: no weight in the merge
+                continue
             for l in range(L):
                 ref = rc.fused(q[0, l], l, nq, nkv, seq_range=(bounds[p], bounds[p + 1]))
                 assert_close(parts[p, l * nq:(l + 1) * nq].cpu().numpy().reshape(-1), ref,
