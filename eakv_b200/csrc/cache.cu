@@ -96,7 +96,9 @@ eakv_cache_t *eakv_cache_create(int n_layers, int n_kv_heads, int head_dim,
   c->geom.n_layers = n_layers;
   c->geom.nib_bytes = (uint32_t)(kPagePositions * c->geom.gpd * 32);
   c->geom.page_bytes = (uint32_t)(kPagePositions * c->geom.gpd * 40);
-  c->buf_bytes = (size_t)n_layers * 2 * n_kv_heads * c->geom.n_pages * c->geom.page_bytes;
+  c->geom.vexp_offset =
+      ((size_t)n_layers * 2 * n_kv_heads * c->geom.n_pages * c->geom.page_bytes + 255) & ~(size_t)255;
+  c->buf_bytes = c->geom.gpd ? c->geom.vexp_offset + (size_t)n_layers * n_kv_heads * sizeof(int) : 0;
   if (cudaGetDevice(&c->device) != cudaSuccess) {
     check_cuda(cudaGetLastError(), "create: no CUDA device");
     free(c);

@@ -18,8 +18,9 @@
 // * The f32 operands (scaled queries; probabilities times V scale) are split
 //   into two f16 limbs, hi = f16(x) and lo = f16(x - hi), which carry ~22
 //   bits; the tensor core accumulates in f32. Queries are pre-scaled per
-//   head by a power of two, and P' per group by 2^-E with E the running max
-//   exponent of the V scales, so both stay inside the f16 range.
+//   head by a power of two, and P' by 2^-E with E the largest exponent of
+//   any V scale of the (layer, head) (kept by the cache), so both stay
+//   inside the f16 range.
 // * Row r = limb*8 + u of the score tile: rows g and g+8 of a thread are the
 //   two limbs of the same (group, head), so a thread adds them in place.
 // * The dimension order inside a k-step is chosen so that a thread's two
@@ -236,12 +237,13 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
       for (int r = 0; r < 4; r++) dv[i][n][r] = 0.0f;
   float m_run = -INFINITY, l_run = 0.0f;
   float pb[NG];
-  int vexp[NG];   // running max biased exponent of the V scales, per group
 #pragma unroll
-  for (int gg = 0; gg < NG; gg++) {
-    pb[gg] = 0.0f;
-    vexp[gg] = -1;
-  }
+  for (int gg = 0; gg < NG; gg++) pb[gg] = 0.0f;
+  // Every V scale of this (layer, head) is below 2^(vexp - 126) (the cache's
+  // exponent table), so P' = p * s * 2^(127 - vexp) < 2 p <= 512 stays in f16.
+  const int vexp = min(max(vexp_table(batch.base[it.b], a.geom)[it.layer * a.geom.n_heads + it.h], 1),
+                       253);
+  const float fs = __uint_as_float((uint32_t)(254 - vexp) << 23);   // 2^(127 - vexp)
   // head of each P'/output column this thread holds: n = 2c + e
   int hcol[2];
 #pragma unroll
@@ -362,25 +364,6 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
     // ---- P' fragments and the V contraction, group by group ------------------
 #pragma unroll
     for (int gg = 0; gg < NG; gg++) {
-      // largest V scale of the step (scales are >= 0: compare as floats)
-      float smax = fmaxf(fmaxf(sv[0][gg], sv[1][gg]), fmaxf(sv[2][gg], sv[3][gg]));
-      smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, 1));
-      smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, 2));
-      const int ex = min(max((int)(__float_as_uint(smax) >> 23) & 0xFF, 1), 253);
-      if (ex > vexp[gg]) {   // warp-uniform: every lane holds the same positions
-        if (vexp[gg] >= 0) {
-          const int dd = ex - vexp[gg];
-          const float f = dd > 126 ? 0.0f : __uint_as_float((uint32_t)(127 - dd) << 23);
-#pragma unroll
-          for (int j = 0; j < 4; j++)
-#pragma unroll
-            for (int n = 0; n < C::VNT; n++)
-#pragma unroll
-              for (int r = 0; r < 4; r++) dv[4 * gg + j][n][r] *= f;
-        }
-        vexp[gg] = ex;
-      }
-      const float fs = __uint_as_float((uint32_t)(254 - vexp[gg]) << 23);   // 2^(127 - vexp)
       float ps[4];
 #pragma unroll
       for (int j = 0; j < 4; j++) {
@@ -483,7 +466,7 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
     for (int mv = 0; mv < C::VMT; mv++) {
       const int gg = mv >> 2, j = mv & 3;
       // undo the 2^(127 - vexp) applied to P': multiply by 2^(vexp - 127)
-      const float vs = __uint_as_float((uint32_t)(vexp[gg] < 0 ? 127 : vexp[gg]) << 23);
+      const float vs = __uint_as_float((uint32_t)vexp << 23);
       const int dlo = 64 * gg + 4 * g + j, dhi = dlo + 32;
 #pragma unroll
       for (int e = 0; e < 2; e++) {

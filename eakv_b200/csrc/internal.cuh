@@ -38,7 +38,27 @@ struct PageGeom {
   int n_layers;
   uint32_t nib_bytes;   // nibble bytes of one page
   uint32_t page_bytes;  // nibbles + (scale, bias) pairs of one page
+  size_t vexp_offset;   // byte offset of the V-scale exponent table in the slab
 };
+
+// Behind the pages each slab keeps int32 vexp[layer][head]: the largest
+// biased f32 exponent of any V scale ever written for that (layer, head).
+// Every writer (quantize, file load) raises it; nothing lowers it, so after
+// restore() or clear() it is still an upper bound. The tensor-core decode
+// reads it once per CTA to scale probability x V-scale operands into the
+// f16 range.
+__host__ __device__ inline int *vexp_table(uint8_t *slab, const PageGeom &g) {
+  return reinterpret_cast<int *>(slab + g.vexp_offset);
+}
+__host__ __device__ inline const int *vexp_table(const uint8_t *slab, const PageGeom &g) {
+  return reinterpret_cast<const int *>(slab + g.vexp_offset);
+}
+
+// Raise vexp[idx] to e (reads first so that the common case is a plain load).
+__device__ inline void vexp_raise(int *vexp, int idx, float scale) {
+  const int e = (int)((__float_as_uint(scale) >> 23) & 0xFF);
+  if (e > *reinterpret_cast<volatile int *>(vexp + idx)) atomicMax(vexp + idx, e);
+}
 
 __host__ __device__ inline size_t page_index(const PageGeom &g, int layer, int kv,
                                              int head, int page) {

@@ -62,7 +62,10 @@ __global__ void pack_kernel(uint8_t *pages, PageGeom g, int layer, int kv, int s
       }
     } else {
       pp[(size_t)slot * 32 + lane] = w[gi * 32 + lane];
-      if (lane == 0) *sb = make_float2(sc[gi], bi[gi]);
+      if (lane == 0) {
+        *sb = make_float2(sc[gi], bi[gi]);
+        if (kv == 1) vexp_raise(vexp_table(pages, g), layer * g.n_heads + h, sc[gi]);
+      }
     }
   }
 }

@@ -144,8 +144,12 @@ quantize_kernel(const float *__restrict__ src, uint8_t *__restrict__ dst, PageGe
       uint8_t *pp = dst + ((size_t)(unit_base + u) * g.n_pages + page) * g.page_bytes;
       const int slot = pip * g.gpd + grp;
       *reinterpret_cast<uint32_t *>(pp + (size_t)slot * 32 + 4 * j) = word;
-      if (j == 0)
+      if (j == 0) {
         *reinterpret_cast<float2 *>(pp + g.nib_bytes + (size_t)slot * 8) = make_float2(scale, mn);
+        const int U = unit_base + (int)u;              // (layer * 2 + kv) * heads + head
+        const int lkv = U / g.n_heads;
+        if (lkv & 1) vexp_raise(vexp_table(dst, g), (lkv >> 1) * g.n_heads + (U - lkv * g.n_heads), scale);
+      }
     }
   }
 }
