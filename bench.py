@@ -44,8 +44,10 @@ CONFIGS = {
             S=2048, B=1),
     2: dict(workload="cfg2 TinyLlama-1.1B GQA 8:1 d64 S2048 B1", L=22, nq=32, nkv=4, hd=64,
             S=2048, B=1),
-    3: dict(workload="cfg3 Llama-2-7B MHA d128 S8192 B1", L=32, nq=32, nkv=32, hd=128,
-            S=8192, B=1),
+    # each step first quantize-appends one new token of every layer and K/V
+    # (restore to S-1, append, advance) and then attends all S positions
+    3: dict(workload="cfg3 Llama-2-7B MHA d128 S8192 B1 + 1-token append per step", L=32,
+            nq=32, nkv=32, hd=128, S=8192, B=1, append=True),
     4: dict(workload="cfg4 Llama-3-8B GQA 4:1 d128 S32768 B16", L=32, nq=32, nkv=8, hd=128,
             S=32768, B=16),
     # multi-GPU: every rank holds a page-aligned slice of every sequence; the
@@ -269,7 +271,18 @@ def config_json(cfg, world):
             "parallelism": (f"sp{world} (sequence split, NCCL all-gather + LSE merge)" if split
                             else f"dp{world} (independent sequences per GPU)"),
             "bytes_per_kv_token": bytes_per_token(cfg),
-            "l2": "inputs larger than L2 (Q4 cache >> 126 MB), no flush"}
+            "l2": ("L2 flushed before every timed step (512 MB device write, outside the "
+                   "timed events)" if needs_flush(cfg) else
+                   "inputs larger than L2 (Q4 cache >> 126 MB), no flush")}
+
+
+L2_BYTES = 126 << 20
+
+
+def needs_flush(cfg):
+    """Caches that fit a few times into L2 would be read from L2 on the next
+    step; those configs flush it between timed steps."""
+    return cfg["B"] * cfg["S"] * bytes_per_token(cfg) < 4 * L2_BYTES
 
 
 def build_caches(E, torch, cfg, device, seed, S=None):
@@ -334,7 +347,22 @@ def run_b200(args, cfg, world, rank, local):
         decoder = SeqSplitDecoder(caches, nq, hd)
         launches_per_step += 1   # the merge kernel
 
-    def step(q_in, o):
+    appending = bool(cfg.get("append"))
+    if appending:
+        S_full = caches[0].seq_len
+        new_kv = torch.randn(L, 2, cfg["nkv"], 1, hd, device=dev)
+        for c in caches:
+            c.set_stream(sh)
+        launches_per_step += 1   # the one-launch append of every layer and K/V
+
+    def step(q_in, o, mid=None):
+        if appending:
+            for c in caches:
+                c.restore(S_full - 1)
+                c.append_step_device(new_kv, 1)
+                c.advance(1)
+            if mid is not None:
+                mid.record(stream)   # decode launch time = this event -> step end
         if split:
             decoder.step(q_in.view(B * L * nq, hd), o.view(B * L * nq, hd), stream=stream)
         else:
@@ -362,17 +390,33 @@ def run_b200(args, cfg, world, rank, local):
     mark = clocks.mark()
     torch.cuda.synchronize()
     barrier()
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev) if needs_flush(cfg) else None
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
-    evs[0].record(stream)
-    for i in range(args.steps):
-        step(qs[i % 4], out)
-        evs[i + 1].record(stream)
+    mids = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)] if appending \
+        else [None] * args.steps
+    if flush is None:
+        evs[0].record(stream)
+        for i in range(args.steps):
+            step(qs[i % 4], out, mids[i])
+            evs[i + 1].record(stream)
+        begins = evs[:-1]
+    else:
+        # each step timed on its own, after an L2 flush outside its events
+        begins = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            begins[i].record(stream)
+            step(qs[i % 4], out, mids[i])
+            evs[i + 1].record(stream)
     torch.cuda.synchronize()
     barrier()
     clk = clocks.stop(mark)
-    per = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
-    total_ms = evs[0].elapsed_time(evs[-1])
-    ms_step = max_over_ranks(total_ms / args.steps)
+    steps_ms = [begins[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    if appending:
+        per = [mids[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    else:
+        per = steps_ms
+    ms_step = max_over_ranks(sum(steps_ms) / args.steps)
     avg_launch_ms = max_over_ranks(sum(per) / len(per))
     status = E.device_status(local)
 
@@ -382,7 +426,17 @@ def run_b200(args, cfg, world, rank, local):
     qh, oh = qh_t.numpy(), oh_t.numpy()
     qd = torch.empty(B, L, nq, hd, device=dev)
 
+    if appending:
+        kv_host = torch.randn(L, 2, cfg["nkv"], 1, hd, pin_memory=True)
+
     def step_host():
+        if appending:
+            # the new token arrives from the host like the query does
+            new_kv.copy_(kv_host, non_blocking=True)
+            for c in caches:
+                c.restore(S_full - 1)
+                c.append_step_device(new_kv, 1)
+                c.advance(1)
         if split:
             qd.copy_(qh_t, non_blocking=True)
             step(qd, out)
@@ -395,14 +449,27 @@ def run_b200(args, cfg, world, rank, local):
         step_host()
     torch.cuda.synchronize()
     barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        step_host()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    if flush is None:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step_host()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_total = e0.elapsed_time(e1)
+    else:
+        e2e_total = 0.0
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            step_host()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            e2e_total += e0.elapsed_time(e1)
+    e2e_ms = max_over_ranks(e2e_total / args.steps)
     assert np.isfinite(oh).all()
 
     tokens_step = B * cfg["S"] * (1 if split else world)
@@ -434,7 +501,9 @@ def run_b200(args, cfg, world, rank, local):
                     "K scale, 4-slice pool rotated over caches/layers)",
             "config": config_json(cfg, world),
             "e2e": {"value": tokens_step / (e2e_ms / 1e3), "unit": UNIT,
-                    "h2d_bytes_per_step": int(qh.nbytes), "d2h_bytes_per_step": int(oh.nbytes),
+                    "h2d_bytes_per_step": int(qh.nbytes) + (int(kv_host.numel()) * 4
+                                                            if appending else 0),
+                    "d2h_bytes_per_step": int(oh.nbytes),
                     "api": "eakv_decode_attention_host"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
