@@ -46,18 +46,19 @@ quantize_kernel(const float *__restrict__ src, uint8_t *__restrict__ dst, PageGe
   const int j = lane & 7;                 // thread within the group
   const long long warps = (long long)gridDim.x * (kThreads / 32);
   const long long warp_id = (long long)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
+  // Largest V-scale exponent this group leader has produced for the
+  // (layer, head) entry v_idx, published to the cache's exponent table when
+  // the entry changes and at the end (one atomic per run of groups instead
+  // of one per group).
+  int v_idx = -1, v_e = 0;
 
-  for (long long gb = warp_id * 4; gb < n_groups; gb += warps * 4) {
-    const long long gi = gb + (lane >> 3);
-    const bool valid = gi < n_groups;
-    float v[8];
-    long long u = 0, gih = 0;
-    if (valid) {
-      // Group gih of unit u: the reference quantizes n_tok*gpd consecutive
-      // 64-float groups starting at the unit's first element
-      // (src/cache.c:78,85-88 and :136-142).
-      u = gi / groups_per_unit;
-      gih = gi - u * groups_per_unit;
+  // Group gih of unit u: the reference quantizes n_tok*gpd consecutive
+  // 64-float groups starting at the unit's first element
+  // (src/cache.c:78,85-88 and :136-142).
+  auto load = [&](long long gi, float (&v)[8]) {
+    if (gi < n_groups) {
+      const long long u = gi / groups_per_unit;
+      const long long gih = gi - u * groups_per_unit;
       const float *x = src + (size_t)u * n_tok * head_dim + (size_t)gih * 64;
       if (kVec) {
         float4 a = *reinterpret_cast<const float4 *>(x + 4 * j);
@@ -75,6 +76,21 @@ quantize_kernel(const float *__restrict__ src, uint8_t *__restrict__ dst, PageGe
 #pragma unroll
       for (int e = 0; e < 8; e++) v[e] = 0.0f;
     }
+  };
+
+  // each iteration loads the next group before it quantizes this one, so
+  // two loads per thread are in flight
+  float nxt[8];
+  load(warp_id * 4 + (lane >> 3), nxt);
+  for (long long gb = warp_id * 4; gb < n_groups; gb += warps * 4) {
+    const long long gi = gb + (lane >> 3);
+    const bool valid = gi < n_groups;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) v[e] = nxt[e];
+    if (gb + warps * 4 < n_groups) load(gi + warps * 4, nxt);
+    const long long u = valid ? gi / groups_per_unit : 0;
+    const long long gih = gi - u * groups_per_unit;
 
     float mn = v[0], mx = v[0];
 #pragma unroll
@@ -148,10 +164,21 @@ quantize_kernel(const float *__restrict__ src, uint8_t *__restrict__ dst, PageGe
         *reinterpret_cast<float2 *>(pp + g.nib_bytes + (size_t)slot * 8) = make_float2(scale, mn);
         const int U = unit_base + (int)u;              // (layer * 2 + kv) * heads + head
         const int lkv = U / g.n_heads;
-        if (lkv & 1) vexp_raise(vexp_table(dst, g), (lkv >> 1) * g.n_heads + (U - lkv * g.n_heads), scale);
+        if (lkv & 1) {
+          const int idx = (lkv >> 1) * g.n_heads + (U - lkv * g.n_heads);
+          const int e = (int)((__float_as_uint(scale) >> 23) & 0xFF);
+          if (idx != v_idx) {
+            if (v_idx >= 0) atomicMax(vexp_table(dst, g) + v_idx, v_e);
+            v_idx = idx;
+            v_e = e;
+          } else {
+            v_e = max(v_e, e);
+          }
+        }
       }
     }
   }
+  if (v_idx >= 0) atomicMax(vexp_table(dst, g) + v_idx, v_e);
 }
 
 }  // namespace
@@ -162,12 +189,21 @@ cudaError_t launch_quantize(const PageGeom &g, uint8_t *d_buf, const float *d_sr
   if (g.gpd <= 0 || n_units <= 0 || n_tok <= 0) return cudaSuccess;
   const long long n_groups = (long long)n_units * n_tok * g.gpd;
   long long blocks = (n_groups + 31) / 32;
-  int dev = 0, sms = 148;
+  const bool vec = ((uintptr_t)d_src & 15) == 0 && (head_dim & 3) == 0;
+  // one wave of resident blocks: the grid-stride loop gives every block the
+  // same share, so blocks beyond the resident set would run as a second,
+  // mostly idle wave
+  int dev = 0, sms = 148, per_sm = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  long long cap = (long long)sms * 8;
+  cudaError_t e = vec ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                            &per_sm, quantize_kernel<true>, kThreads, 0)
+                      : cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                            &per_sm, quantize_kernel<false>, kThreads, 0);
+  if (e != cudaSuccess) return e;
+  const long long cap = (long long)sms * (per_sm > 0 ? per_sm : 1);
   if (blocks > cap) blocks = cap;
-  if (((uintptr_t)d_src & 15) == 0 && (head_dim & 3) == 0)
+  if (vec)
     quantize_kernel<true><<<(int)blocks, kThreads, 0, s>>>(d_src, d_buf, g, unit_base, n_groups,
                                                            n_tok, pos0, head_dim);
   else
