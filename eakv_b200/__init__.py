@@ -78,6 +78,7 @@ SIGNATURES = {
     "eakv_lse_combine": (_I, [_I, _I, _I, _P, _P, _P, _P, _P]),
     "eakv_test_force_splits": (_I, [_I]),
     "eakv_test_force_path": (_I, [_I]),
+    "eakv_test_stall": (_I, [_I, ctypes.c_uint]),
 }
 
 _lib = None
@@ -329,3 +330,9 @@ def force_splits(n):
 def force_path(path):
     """1: CUDA-core decode kernel for every shape; 0: automatic choice."""
     lib().eakv_test_force_path(int(path))
+
+
+def test_stall(page, wait_budget=0):
+    """Failure-detection aid: decode kernels never request `page` of a work
+    item (page < 0: off) and give up each wait after `wait_budget` polls."""
+    lib().eakv_test_stall(int(page), int(wait_budget))

@@ -15,6 +15,9 @@ __device__ int g_status;
 thread_local int t_force_splits = 0;
 // Kernel path forced by eakv_test_force_path() on this host thread.
 thread_local int t_force_path = 0;
+// Stalled page and wait budget set by eakv_test_stall() on this host thread.
+thread_local int t_test_stall = 0;
+thread_local unsigned t_wait_budget = 0;
 
 int *device_status_ptr() {
   static int *ptrs[64] = {nullptr};
@@ -83,6 +86,8 @@ DecodeArgs base_args(const eakv_cache_t *c0, int n_caches, int n_q) {
   a.status = device_status_ptr();
   a.force_splits = t_force_splits;
   a.force_path = t_force_path;
+  a.test_stall = t_test_stall;
+  a.wait_budget = t_wait_budget;
   return a;
 }
 
@@ -298,5 +303,11 @@ extern "C" int eakv_test_force_path(int path) {
 
 extern "C" int eakv_test_force_splits(int n) {
   eakv::t_force_splits = n > 0 ? n : 0;
+  return EAKV_OK;
+}
+
+extern "C" int eakv_test_stall(int page, unsigned wait_budget) {
+  eakv::t_test_stall = page >= 0 ? page + 1 : 0;
+  eakv::t_wait_budget = wait_budget;
   return EAKV_OK;
 }

@@ -113,6 +113,7 @@ decode_simt_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
     for (int s = 0; s < C::NSTAGE; s++) {
       mbar_init(smem_u32(&bars[s]), 1);                               // stage filled
       reinterpret_cast<int *>(&bars[C::NSTAGE])[s] = 0;               // release count
+      reinterpret_cast<int *>(&bars[C::NSTAGE])[C::NSTAGE + s] = -1;  // last page requested
     }
     fence_mbar_init();
   }
@@ -120,13 +121,16 @@ decode_simt_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
 
   // Thread 0 fills the first NSTAGE stages; afterwards the last warp to
   // release a stage refills it (no thread ever waits for a stage to drain).
+  int *last_req = reinterpret_cast<int *>(&bars[C::NSTAGE]) + C::NSTAGE;
   auto issue = [&](int i) {
+    if (i == a.test_stall - 1) return;   // test hook: this stage's wait runs out
     const int st = i % C::NSTAGE;
     const uint32_t full = smem_u32(&bars[st]);
     mbar_arrive_expect_tx(full, 2 * C::PB);
     const uint32_t dst = smem_u32(smem + st * C::STAGE_BYTES);
     bulk_g2s(dst, kpages + (size_t)(it.pg0 + i) * C::PB, C::PB, full);
     bulk_g2s(dst + C::PB, vpages + (size_t)(it.pg0 + i) * C::PB, C::PB, full);
+    last_req[st] = i;
   };
   if (threadIdx.x == 0)
     for (int i = 0; i < it.npages && i < C::NSTAGE; i++) issue(i);
@@ -175,7 +179,7 @@ decode_simt_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
   bool ok = true;
   for (int i = 0; i < it.npages; i++) {
     const int st = i % C::NSTAGE;
-    if (!ok || !mbar_wait(smem_u32(&bars[st]), (i / C::NSTAGE) & 1)) {
+    if (!ok || !mbar_wait(smem_u32(&bars[st]), (i / C::NSTAGE) & 1, a.wait_budget)) {
       atomicOr(a.status, kStatusWaitTimeout);
       ok = false;
       break;
@@ -275,7 +279,10 @@ decode_simt_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
       issue(i + C::NSTAGE);
   }
   // every wait above is bounded, so all threads get here; leave together
-  if (!__syncthreads_and(ok)) return;
+  if (!__syncthreads_and(ok)) {
+    if (threadIdx.x == 0) drain_stages(bars, last_req, C::NSTAGE, a.wait_budget);
+    return;
+  }
 
   // ---- reduce the warp's position slots --------------------------------
 #pragma unroll
@@ -504,6 +511,7 @@ size_t decode_workspace_bytes(const DecodeArgs &a0, const DecodeBatch &batch) {
 int decode_launch(const DecodeArgs &a0, const DecodeBatch &batch, void *workspace,
                   size_t workspace_bytes, cudaStream_t s) {
   DecodeArgs a = a0;
+  if (a.wait_budget == 0) a.wait_budget = kWaitBudget;
   const Plan p = plan(a, batch);
   if (a.n_splits > 1) {
     size_t rows = (size_t)a.n_caches * a.n_layers * a.n_q_heads;

@@ -1,33 +1,43 @@
 // decode_mma.cu - fused softmax attention over the Q4 cache on the tensor
-// cores (mma.sync m16n8k16, f16 operands, f32 accumulation), for GQA groups
-// of 4 or 8 query heads per KV head.
+// cores (mma.sync), for GQA groups of 4 or 8 query heads per KV head.
 //
 // Same work decomposition, page pipeline and merge as the CUDA-core kernel
 // in decode.cu; what changes is how the two contractions of a position
 // block are evaluated. Per warp and 16-position step:
 //
-//   S[(group, head, limb)][pos]  = Qlimbs[16 x 16 dims] * Knib[16 dims x 8 pos]   (x 8 k-steps)
-//   O[dims][(head, limb)]       += Vnib[16 dims x 16 pos] * P'[16 pos x (head, limb)]
+//   S[(head, limb)][pos] = Qdigits[16 x 32 dims] * Knib[32 dims x 8 pos]   (int8, per group)
+//   O[dims][(head, limb)] += Vnib[16 dims x 16 pos] * P'[16 pos x (head, limb)]   (f16)
 //
-// * The nibbles (0..15) are exact in f16. They are turned into f16 pairs in
-//   registers with one mask+or and one f16 subtract each: placing a nibble
-//   in the low mantissa bits of 1024.0 (0x6400) and subtracting 1024 gives
-//   it exactly; a high nibble is taken in place (bits 4..7), i.e. times 16,
-//   and the 1/16 is folded into the matching query element (K) or applied
-//   to the output row (V).
-// * The f32 operands (scaled queries; probabilities times V scale) are split
-//   into two f16 limbs, hi = f16(x) and lo = f16(x - hi), which carry ~22
-//   bits; the tensor core accumulates in f32. Queries are pre-scaled per
-//   head by a power of two, and P' by 2^-E with E the largest exponent of
-//   any V scale of the (layer, head) (kept by the cache), so both stay
-//   inside the f16 range.
-// * Row r = limb*8 + u of the score tile: rows g and g+8 of a thread are the
-//   two limbs of the same (group, head), so a thread adds them in place.
-// * The dimension order inside a k-step is chosen so that a thread's two
-//   f16x2 B registers come from one 32-bit word of its position's nibble
-//   row; the query fragments are permuted the same way once per CTA.
-// * Scales and biases are applied in f32 outside the tensor core:
-//     score = s_k * dot + b_k * sum(q), O += (p s_v) n + p b_v.
+// Scores (integer tensor cores, mma m16n8k32 s8 x u8 -> s32):
+// * Each query is written as a fixed-point integer x = rn(q 2^E) with
+//   |x| <= 2^30 (E per head from its largest |q|), split into four signed
+//   base-256 digits x = d0 + 2^8 d1 + 2^16 d2 + 2^24 d3 (each in [-128, 127]).
+//   The (head, digit) pairs are the 16 rows of an m-tile.
+// * The K nibbles enter the tensor core as they are stored: a 32-bit word of
+//   a position's row holds four bytes; w & 0x0F0F0F0F are four low nibbles
+//   (dims b..b+3) and w & 0xF0F0F0F0 four high nibbles times 16 (dims
+//   b+32..b+35), whose queries are taken as rn(q 2^(E-4)) instead. One
+//   logic op per four nibbles, no conversion.
+// * Every product and sum is exact in the s32 accumulator (|digit * nibble|
+//   sums over a 64-dim group stay below 2^21). A thread holds two digit rows
+//   of one head; it joins them exactly in integers (t = D_l + 256 D_l+1 <
+//   2^29), converts once, and (for 4 heads per CTA) adds the partner
+//   thread's other two digits with one shuffle.
+// * Each 64-dim group has its own accumulator, so the group's scale and
+//   bias apply in f32 afterwards: score = s_k * dot + b_k * sum(q).
+//
+// Outputs (f16 tensor cores, mma m16n8k16 f16 -> f32):
+// * The V nibbles (0..15) are exact in f16. They are turned into f16 pairs
+//   in registers with one mask+or and one f16 subtract each: placing a
+//   nibble in the low mantissa bits of 1024.0 (0x6400) and subtracting 1024
+//   gives it exactly; a high nibble is taken in place (bits 4..7), i.e.
+//   times 16, and the 1/16 is applied to the output row.
+// * P' = p * s_v (a probability times the V scale) is split into two f16
+//   limbs, hi = f16(x) and lo = f16(x - hi), which carry ~22 bits; the
+//   tensor core accumulates in f32. P' is prescaled by 2^-E with E the
+//   largest exponent of any V scale of the (layer, head) (kept by the
+//   cache), so it stays inside the f16 range. The bias part p * b_v is
+//   accumulated in f32 outside the tensor core.
 // * Online softmax in base 2 with a lazy maximum: the running max moves only
 //   when a block's max exceeds it by more than 8, so probabilities stay in
 //   [0, 256] and rescaling the accumulators is rare.
@@ -46,8 +56,8 @@ namespace {
 template <int HD, int GH>
 struct MCfg {
   static constexpr int NG = HD / 64;                        // groups per position
-  static constexpr int KS = 4 * NG;                         // K k-steps of 16 dims
-  static constexpr int KMT = (GH == 8 && NG == 2) ? 2 : 1;  // score m-tiles (one per group)
+  static constexpr int KSG = 2;                             // score k-steps (32 dims) per group
+  static constexpr int KMT = GH / 4;                        // score m-tiles (4 heads x 4 digits)
   static constexpr int VNT = GH == 8 ? 2 : 1;               // P' n-tiles (one per limb)
   static constexpr int VMT = 4 * NG;                        // output m-tiles of 16 dims
   static constexpr int NW = 4;                              // warps; each takes 16 positions of a page
@@ -89,11 +99,6 @@ __device__ __forceinline__ uint32_t nib_pair(uint32_t w, uint32_t mask) {
   return f16x2_sub1024(and_or(w, mask, kMagic));
 }
 
-__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
-  __half2 h = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<uint32_t *>(&h);
-}
-
 // x = hi + lo in two f16 limbs: limb 0 = f16(x), limb 1 = f16(x - f16(x)).
 __device__ __forceinline__ void split2(float x0, float x1, uint32_t &h, uint32_t &l) {
   __half2 hh = __floats2half2_rn(x0, x1);
@@ -112,16 +117,26 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Dimension (and its weight, 1 or 16) that K slot kk of k-step ks stands for.
-// Thread c of a position row holds bytes [8c, 8c+8) of each group as two
-// words; even k-steps use bytes 0/2 of a word, odd ones bytes 1/3; slots
-// 0..7 take low nibbles, 8..15 high nibbles (weight 16).
-__device__ __forceinline__ int kdim(int ks, int kk, int &weight) {
-  const int grp = ks >> 2, kl = ks & 3, m = kl >> 1, odd = kl & 1;
-  const int cc = (kk & 7) >> 1, e = kk & 1, second = kk >> 3;
-  const int byte = 8 * cc + 4 * m + odd + 2 * e;
-  weight = second ? 16 : 1;
-  return 64 * grp + byte + (second ? 32 : 0);
+__device__ __forceinline__ void imma16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                          uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Signed base-256 digit l (0..3) of x, |x| <= 2^30: x = sum_l digit_l 2^(8l)
+// with every digit in [-128, 127].
+__device__ __forceinline__ int digit(int x, int l) {
+  int d = 0;
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    d = (int)(int8_t)(x & 0xFF);
+    if (k == l) break;
+    x = (x - d) >> 8;
+  }
+  return d;
 }
 
 template <int HD, int GH>
@@ -146,32 +161,33 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
     for (int s = 0; s < C::NSTAGE; s++) {
       mbar_init(smem_u32(&bars[s]), 1);                               // stage filled
       reinterpret_cast<int *>(&bars[C::NSTAGE])[s] = 0;               // release count
+      reinterpret_cast<int *>(&bars[C::NSTAGE])[C::NSTAGE + s] = -1;  // last page requested
     }
     fence_mbar_init();
   }
   __syncthreads();
+  int *last_req = reinterpret_cast<int *>(&bars[C::NSTAGE]) + C::NSTAGE;
   auto issue = [&](int i) {
+    if (i == a.test_stall - 1) return;   // test hook: this stage's wait runs out
     const int st = i % C::NSTAGE;
     const uint32_t full = smem_u32(&bars[st]);
     mbar_arrive_expect_tx(full, 2 * C::PB);
     const uint32_t dst = smem_u32(smem + st * C::STAGE_BYTES);
     bulk_g2s(dst, kpages + (size_t)(it.pg0 + i) * C::PB, C::PB, full);
     bulk_g2s(dst + C::PB, vpages + (size_t)(it.pg0 + i) * C::PB, C::PB, full);
+    last_req[st] = i;
   };
   if (threadIdx.x == 0)
     for (int i = 0; i < it.npages && i < C::NSTAGE; i++) issue(i);
 
   // ---- per-thread query fragments -----------------------------------------
-  // (group, head) of this thread's score rows, for each score m-tile
   const int qh0 = it.h * G + it.hg * GH;
   const float *qb = a.q + ((size_t)(it.b * a.n_layers + it.lrow) * a.n_q_heads + qh0) * HD;
-  auto row_pair = [&](int mt, int &grp_r, int &h_r) {
-    const int pi = (NG * GH >= 8) ? (mt * 8 + g) : (g % (NG * GH));
-    grp_r = pi / GH;
-    h_r = pi % GH;
-  };
-  int h_mine, grp_mine;
-  row_pair(0, grp_mine, h_mine);   // the head this thread scores (same for every m-tile)
+  // Score rows: row g of m-tile mt is (head h_mine, digit l_row + 2 mt),
+  // row g+8 the next digit. With 4 heads, lanes g and g^4 share a head
+  // (digits 0,1 and 2,3); with 8, m-tiles 0 and 1 give lane g all four.
+  const int h_mine = (GH == 4) ? (g & 3) : g;
+  const int l_row = (GH == 4) ? 2 * (g >> 2) : 0;
   const float qscale = rsqrtf((float)HD) * kLog2e;
   // stage the scaled query block; one warp per head computes max|q| and
   // the per-group sums (for the bias term)
@@ -192,40 +208,49 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
     if (lane == 0) stat_s[h] = mx;
   }
   __syncthreads();
-  // per-head power-of-two prescale keeping the query limbs inside f16
+  // fixed point: x = rn(q 2^E) with |x| <= 2^30; E is capped at 126 so that
+  // 2^-E stays a normal float (queries below 2^-96 lose low bits only)
   const float hmax = stat_s[h_mine];
   int qexp = 0;
-  frexpf(hmax > 0.0f ? hmax : 1.0f, &qexp);   // hmax in [2^(qexp-1), 2^qexp)
-  const float q_up = ldexpf(1.0f, 10 - qexp);     // largest |q| -> [512, 1024)
-  const float q_down = ldexpf(1.0f, qexp - 10);
+  frexpf(hmax > 0.0f && hmax <= 3.0e38f ? hmax : 1.0f, &qexp);   // hmax in [2^(qexp-1), 2^qexp)
+  const int qe = min(30 - qexp, 126);
+  const float up_lo = __uint_as_float((uint32_t)(127 + qe) << 23);       // 2^E
+  const float up_hi = __uint_as_float((uint32_t)(127 + qe - 4) << 23);   // 2^(E-4)
+  // weight of this lane's joined digits: 2^(8 l_row - E); a query with an
+  // inf or NaN element turns every score of its head into NaN
+  const float w_row = (hmax <= 3.0e38f) ? __uint_as_float((uint32_t)(127 + 8 * l_row - qe) << 23)
+                                        : __uint_as_float(0x7fc00000u);
 
-  uint32_t aq[C::KS][4];
+  // A fragments: k-step ks of group gg, lane c holds dims 64 gg + 8c + 4ks + i
+  // (low nibbles, bytes i of its K word) and the same + 32 (high nibbles)
+  uint32_t aq[NG][C::KSG][C::KMT][4];
 #pragma unroll
-  for (int ks = 0; ks < C::KS; ks++) {
-    const int mt = (C::KMT == 2) ? (ks >> 2) : 0;
-    int grp_r, h_r;
-    row_pair(mt, grp_r, h_r);
-    const bool live = grp_r == (ks >> 2);
-    float v[4];
+  for (int gg = 0; gg < NG; gg++)
 #pragma unroll
-    for (int s = 0; s < 4; s++) {   // slots 2c, 2c+1, 2c+8, 2c+9
-      const int kk = 2 * c + (s & 1) + (s >> 1) * 8;
-      int w;
-      const int d = kdim(ks, kk, w);
-      v[s] = live ? q_s[h_r * HD + d] * (q_up / (float)w) : 0.0f;
-    }
-    uint32_t h01, l01, h23, l23;
-    split2(v[0], v[1], h01, l01);
-    split2(v[2], v[3], h23, l23);
-    aq[ks][0] = h01;   // row g   (limb 0), slots 2c, 2c+1
-    aq[ks][1] = l01;   // row g+8 (limb 1)
-    aq[ks][2] = h23;   // row g,   slots 2c+8, 2c+9
-    aq[ks][3] = l23;
-  }
-  // sum of the (unscaled by q_up) query over each group's dims, for the bias
+    for (int ks = 0; ks < C::KSG; ks++)
+#pragma unroll
+      for (int mt = 0; mt < C::KMT; mt++) {
+        const int l0 = l_row + 2 * mt;
+        uint32_t r[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const int d = 64 * gg + 8 * c + 4 * ks + i;
+          const int xl = __float2int_rn(q_s[h_mine * HD + d] * up_lo);
+          const int xh = __float2int_rn(q_s[h_mine * HD + d + 32] * up_hi);
+          r[0] |= (uint32_t)(digit(xl, l0) & 0xFF) << (8 * i);       // row g,   low dims
+          r[1] |= (uint32_t)(digit(xl, l0 + 1) & 0xFF) << (8 * i);   // row g+8, low dims
+          r[2] |= (uint32_t)(digit(xh, l0) & 0xFF) << (8 * i);       // row g,   high dims
+          r[3] |= (uint32_t)(digit(xh, l0 + 1) & 0xFF) << (8 * i);   // row g+8, high dims
+        }
+#pragma unroll
+        for (int k = 0; k < 4; k++) aq[gg][ks][mt][k] = r[k];
+      }
+  // per-group query sums for the bias term; with 4 heads only the lane
+  // holding digits 0,1 adds it (its partner's share arrives by shuffle)
   float qsum[NG];
 #pragma unroll
-  for (int gg = 0; gg < NG; gg++) qsum[gg] = stat_s[GH + h_mine * NG + gg];
+  for (int gg = 0; gg < NG; gg++)
+    qsum[gg] = (GH == 4 && l_row) ? 0.0f : stat_s[GH + h_mine * NG + gg];
 
   // ---- accumulators -----------------------------------------------------------
   float dv[C::VMT][C::VNT][4];
@@ -291,24 +316,25 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
     float sc[4];
 #pragma unroll
     for (int tile = 0; tile < 2; tile++) {
-      float dk[C::KMT][4];
+      int dk[NG][C::KMT][4];
 #pragma unroll
-      for (int mt = 0; mt < C::KMT; mt++)
+      for (int gg = 0; gg < NG; gg++)
 #pragma unroll
-        for (int r = 0; r < 4; r++) dk[mt][r] = 0.0f;
+        for (int mt = 0; mt < C::KMT; mt++)
+#pragma unroll
+          for (int r = 0; r < 4; r++) dk[gg][mt][r] = 0;
+      // B fragments: lane (g, c) takes bytes 8c..8c+7 of position g's group row
       const uint8_t *row = ks_ + (p0 + 8 * tile + g) * (HD / 2) + 8 * c;
 #pragma unroll
       for (int gg = 0; gg < NG; gg++) {
         const uint2 wv = *reinterpret_cast<const uint2 *>(row + 32 * gg);
 #pragma unroll
-        for (int kl = 0; kl < 4; kl++) {
-          const int ks = 4 * gg + kl;
-          const uint32_t w = (kl >> 1) ? wv.y : wv.x;
-          const uint32_t y = (kl & 1) ? (w >> 8) : w;
-          const uint32_t b0 = nib_pair(y, 0x000F000Fu);
-          const uint32_t b1 = nib_pair(y, 0x00F000F0u);
-          const int mt = (C::KMT == 2) ? gg : 0;
-          mma16816(dk[mt], aq[ks][0], aq[ks][1], aq[ks][2], aq[ks][3], b0, b1);
+        for (int ks = 0; ks < C::KSG; ks++) {
+          const uint32_t w = ks ? wv.y : wv.x;
+          const uint32_t b0 = w & 0x0F0F0F0Fu;   // low nibbles
+          const uint32_t b1 = w & 0xF0F0F0F0u;   // high nibbles x16
+#pragma unroll
+          for (int mt = 0; mt < C::KMT; mt++) imma16832(dk[gg][mt], aq[gg][ks][mt], b0, b1);
         }
       }
 #pragma unroll
@@ -316,15 +342,16 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
         const int j = 2 * tile + e;
         float part = 0.0f;
 #pragma unroll
-        for (int mt = 0; mt < C::KMT; mt++) {
-          int grp_r, h_r;
-          row_pair(mt, grp_r, h_r);
-          const float dot = (dk[mt][e] + dk[mt][2 + e]) * q_down;
-          const float s_ = (NG == 2 && grp_r) ? sk[j][NG - 1] : sk[j][0];
-          const float b_ = (NG == 2 && grp_r) ? bk[j][NG - 1] : bk[j][0];
-          part += fmaf(dot, s_, b_ * ((NG == 2 && grp_r) ? qsum[NG - 1] : qsum[0]));
+        for (int gg = 0; gg < NG; gg++) {
+          // join the lane's digit rows exactly, then convert once
+          float u = (float)(dk[gg][0][e] + 256 * dk[gg][0][2 + e]);
+          if (C::KMT == 2) u = fmaf((float)(dk[gg][1][e] + 256 * dk[gg][1][2 + e]), 65536.0f, u);
+          part = fmaf(u, sk[j][gg], part);
         }
-        if (NG == 2 && C::KMT == 1) part += __shfl_xor_sync(0xffffffffu, part, 4 * GH);
+        part *= w_row;
+#pragma unroll
+        for (int gg = 0; gg < NG; gg++) part = fmaf(bk[j][gg], qsum[gg], part);
+        if (GH == 4) part += __shfl_xor_sync(0xffffffffu, part, 16);
         sc[j] = (FULL || tval[j]) ? part : -INFINITY;
       }
     }
@@ -408,7 +435,7 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
   bool ok = true;
   for (int i = 0; i < it.npages; i++) {
     const int st = i % C::NSTAGE;
-    if (!ok || !mbar_wait(smem_u32(&bars[st]), (i / C::NSTAGE) & 1)) {
+    if (!ok || !mbar_wait(smem_u32(&bars[st]), (i / C::NSTAGE) & 1, a.wait_budget)) {
       atomicOr(a.status, kStatusWaitTimeout);
       ok = false;
       break;
@@ -426,7 +453,10 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
         i + C::NSTAGE < it.npages)
       issue(i + C::NSTAGE);
   }
-  if (!__syncthreads_and(ok)) return;
+  if (!__syncthreads_and(ok)) {
+    if (threadIdx.x == 0) drain_stages(bars, last_req, C::NSTAGE, a.wait_budget);
+    return;
+  }
 
   // ---- per-warp totals --------------------------------------------------------
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);

@@ -144,6 +144,9 @@ struct DecodeArgs {
   int *status;                      // device status word (bounded waits)
   int force_splits;                 // > 0: use this many splits (tests)
   int force_path;                   // 1: CUDA-core kernel even where tensor cores apply
+  unsigned wait_budget;             // polls per bounded wait (0: the default budget)
+  int test_stall;                   // > 0: page test_stall-1 of every item is never
+                                    // requested, so its wait runs out (tests only)
   // filled by the planner
   int n_splits, split_pages;
   float *part_m, *part_l, *part_o;
@@ -160,5 +163,7 @@ int mma_resident(int gh, int head_dim);
 int mma_launch(int gh, const DecodeArgs &a, const DecodeBatch &b, int n_blocks, cudaStream_t s);
 extern thread_local int t_force_path;
 extern thread_local int t_force_splits;
+extern thread_local int t_test_stall;
+extern thread_local unsigned t_wait_budget;
 
 }  // namespace eakv

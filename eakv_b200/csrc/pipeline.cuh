@@ -46,11 +46,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity to complete.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kWaitBudget; i++)
+// Bounded wait for the phase with the given parity to complete: at most
+// `budget` polls.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t budget) {
+  for (uint32_t i = 0; i < budget; i++)
     if (mbar_try_wait(bar, parity)) return true;
   return false;
+}
+
+// After a wait ran out: wait (bounded again) for the last copy requested
+// into every stage, so that no bulk copy still writes this CTA's shared
+// memory when it exits. last[s] is the page last requested into stage s
+// (-1: none); its phase parity is (last[s] / nstage) & 1, and a phase that
+// completed earlier answers at once.
+__device__ __forceinline__ void drain_stages(const uint64_t *bars, const int *last, int nstage,
+                                             uint32_t budget) {
+  for (int s = 0; s < nstage; s++)
+    if (last[s] >= 0) mbar_wait(smem_u32(&bars[s]), (last[s] / nstage) & 1, budget);
 }
 
 // 1-D bulk copy global -> shared, completion counted in bytes on `bar`.

@@ -152,6 +152,16 @@ int eakv_test_force_splits(int n);
  * side-by-side measurements. */
 int eakv_test_force_path(int path);
 
+/* Failure-detection test: later fused / decode calls on this host thread
+ * never request page `page` of each (row, split) work item into the
+ * pipeline (page < 0 restores normal operation), and every wait of those
+ * kernels gives up after `wait_budget` polls (0: the default budget). The
+ * wait for the missing page then runs out: the kernel sets bit 1 of the
+ * device status word (eakv_device_status), waits for the copies it did
+ * request, and returns without writing its outputs. Nothing faults; the
+ * context stays usable. */
+int eakv_test_stall(int page, unsigned wait_budget);
+
 #ifdef __cplusplus
 }
 #endif
