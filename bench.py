@@ -50,10 +50,12 @@ CONFIGS = {
             nq=32, nkv=32, hd=128, S=8192, B=1, append=True),
     4: dict(workload="cfg4 Llama-3-8B GQA 4:1 d128 S32768 B16", L=32, nq=32, nkv=8, hd=128,
             S=32768, B=16),
-    # multi-GPU: every rank holds a page-aligned slice of every sequence; the
-    # partial (output, LSE) of the ranks are all-gathered over NCCL and merged
-    5: dict(workload="cfg5 Llama-3-70B GQA 8:1 d128 S131072 B4 (sequence split)", L=80,
-            nq=64, nkv=8, hd=128, S=131072, B=4, split=True),
+    # multi-GPU: the KV heads (with their query heads) are sharded over the
+    # GPUs; beyond one KV head per GPU (or with --seq-shards) every rank of a
+    # head shard holds a page-aligned slice of every sequence, and the
+    # partial (output, LSE) of those ranks are all-gathered over NCCL and merged
+    5: dict(workload="cfg5 Llama-3-70B GQA 8:1 d128 S131072 B4 (KV-head shards x sequence "
+            "split)", L=80, nq=64, nkv=8, hd=128, S=131072, B=4, shard=True),
 }
 
 FALLBACK_HBM_GBS = 6650.0
@@ -73,7 +75,8 @@ def measured_peak():
 
 
 def ncu_traffic(kernel_key):
-    """DRAM bytes per KV token of a kernel from the committed ncu summary."""
+    """DRAM bytes per algorithmic byte of a kernel, from the committed ncu
+    summary (a capture whose traffic scales with the pages read)."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
     try:
         with open(p) as f:
@@ -263,13 +266,26 @@ def run_reference(args, cfg, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def config_json(cfg, world):
-    split = bool(cfg.get("split")) and world > 1
+def layout(cfg, world, seq_shards=0):
+    """(head shards, sequence shards) of a sharded config on `world` ranks."""
+    if not cfg.get("shard") or world == 1:
+        return 1, 1
+    from eakv_b200.parallel import shard_layout
+    return shard_layout(world, cfg["nkv"], seq_shards)
+
+
+def config_json(cfg, world, seq_shards=0):
+    hs, ss = layout(cfg, world, seq_shards)
+    sharded = bool(cfg.get("shard"))
+    if sharded:
+        par = (f"kv-head shards x{hs}, sequence split x{ss}"
+               + (" (NCCL all-gather + LSE merge)" if ss > 1 else " (no data-path collective)"))
+    else:
+        par = f"dp{world} (independent sequences per GPU)"
     return {"workload": cfg["workload"], "layers": cfg["L"], "q_heads": cfg["nq"],
             "kv_heads": cfg["nkv"], "head_dim": cfg["hd"], "seq_len": cfg["S"],
-            "batch_per_gpu": cfg["B"], "global_batch": cfg["B"] * (1 if split else world),
-            "parallelism": (f"sp{world} (sequence split, NCCL all-gather + LSE merge)" if split
-                            else f"dp{world} (independent sequences per GPU)"),
+            "batch_per_gpu": cfg["B"], "global_batch": cfg["B"] * (1 if sharded else world),
+            "parallelism": par,
             "bytes_per_kv_token": bytes_per_token(cfg),
             "l2": ("L2 flushed before every timed step (512 MB device write, outside the "
                    "timed events)" if needs_flush(cfg) else
@@ -326,14 +342,25 @@ def run_b200(args, cfg, world, rank, local):
     if args.splits:
         E.force_splits(args.splits)
     dev = torch.device("cuda", local)
-    split = bool(cfg.get("split")) and world > 1
+    # this rank's share: its KV heads (with their query heads) and, under a
+    # sequence split, its slice of every sequence
+    hs, ss = layout(cfg, world, args.seq_shards)
+    lcfg = dict(cfg, nkv=cfg["nkv"] // hs, nq=cfg["nq"] // hs)
+    split = ss > 1
+    sub = None
     if split:
+        import torch.distributed as dist
         from eakv_b200.parallel import SeqSplitDecoder, seq_shard
-        lo, hi = seq_shard(cfg["S"], world, rank)
-        caches = build_caches(E, torch, cfg, dev, seed=1234 + rank, S=hi - lo)
+        # one process group per head shard (every rank creates every group)
+        for h in range(hs):
+            g_ = dist.new_group(ranks=[h * ss + k for k in range(ss)])
+            if h == rank // ss:
+                sub = g_
+        lo, hi = seq_shard(cfg["S"], ss, rank % ss)
+        caches = build_caches(E, torch, lcfg, dev, seed=1234 + rank, S=hi - lo)
     else:
-        caches = build_caches(E, torch, cfg, dev, seed=1234 + rank)
-    B, L, nq, hd = cfg["B"], cfg["L"], cfg["nq"], cfg["hd"]
+        caches = build_caches(E, torch, lcfg, dev, seed=1234 + rank)
+    B, L, nq, hd = lcfg["B"], lcfg["L"], lcfg["nq"], lcfg["hd"]
     # a stream of our own: the legacy default stream has handle 0, which the
     # library reads as "the cache's stream"; events must sit on the stream
     # the kernels run on
@@ -344,13 +371,13 @@ def run_b200(args, cfg, world, rank, local):
     out = torch.empty(B, L, nq, hd, device=dev)
     launches_per_step = E.decode_launches(caches, nq)
     if split:
-        decoder = SeqSplitDecoder(caches, nq, hd)
+        decoder = SeqSplitDecoder(caches, nq, hd, group=sub)
         launches_per_step += 1   # the merge kernel
 
     appending = bool(cfg.get("append"))
     if appending:
         S_full = caches[0].seq_len
-        new_kv = torch.randn(L, 2, cfg["nkv"], 1, hd, device=dev)
+        new_kv = torch.randn(L, 2, lcfg["nkv"], 1, hd, device=dev)
         for c in caches:
             c.set_stream(sh)
         launches_per_step += 1   # the one-launch append of every layer and K/V
@@ -427,7 +454,7 @@ def run_b200(args, cfg, world, rank, local):
     qd = torch.empty(B, L, nq, hd, device=dev)
 
     if appending:
-        kv_host = torch.randn(L, 2, cfg["nkv"], 1, hd, pin_memory=True)
+        kv_host = torch.randn(L, 2, lcfg["nkv"], 1, hd, pin_memory=True)
 
     def step_host():
         if appending:
@@ -472,20 +499,22 @@ def run_b200(args, cfg, world, rank, local):
     e2e_ms = max_over_ranks(e2e_total / args.steps)
     assert np.isfinite(oh).all()
 
-    tokens_step = B * cfg["S"] * (1 if split else world)
+    # whole job: every rank's sequences, or (sharded) each sequence once
+    tokens_step = B * cfg["S"] * (1 if cfg.get("shard") else world)
     value = tokens_step / (ms_step / 1e3)
-    bpt = bytes_per_token(cfg)
+    bpt = bytes_per_token(lcfg)
     # one decode launch per rank covers all of the rank's positions
     alg_bytes_launch = B * (caches[0].seq_len) * bpt
     peak, peak_kind = measured_peak()
     achieved = alg_bytes_launch / (avg_launch_ms / 1e3) / 1e9
-    G = nq // cfg["nkv"]
-    if not args.force_simt and hd in (64, 128) and G % 4 == 0:
-        kname = f"decode_mma_kernel<{hd},{8 if G % 8 == 0 else 4}>"
+    G = nq // lcfg["nkv"]
+    if not args.force_simt and hd in (64, 128):
+        gh = max(d for d in range(1, min(G, 8) + 1) if G % d == 0)   # query heads per CTA
+        kname = f"decode_mma_kernel<{hd},{8 if gh > 4 else 4}>"
     else:
         gc = 8 if G % 8 == 0 else 4 if G % 4 == 0 else 2 if G % 2 == 0 else 1
         kname = f"decode_simt_kernel<{hd},{gc}>"
-    traffic_per_token = ncu_traffic(kname)
+    traffic_ratio = ncu_traffic(kname)
     result = None
     if rank == 0:
         cpu = None
@@ -495,11 +524,11 @@ def run_b200(args, cfg, world, rank, local):
         result = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "higher_is_better": True, "scaling": "strong" if split else "weak",
+            "higher_is_better": True, "scaling": "strong" if cfg.get("shard") else "weak",
             "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded torch.randn K/V on device, per-channel log-uniform[0.5,8] "
                     "K scale, 4-slice pool rotated over caches/layers)",
-            "config": config_json(cfg, world),
+            "config": config_json(cfg, world, args.seq_shards),
             "e2e": {"value": tokens_step / (e2e_ms / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": int(qh.nbytes) + (int(kv_host.numel()) * 4
                                                             if appending else 0),
@@ -507,7 +536,7 @@ def run_b200(args, cfg, world, rank, local):
                     "api": "eakv_decode_attention_host"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
-                         "traffic": (traffic_per_token * B * cfg["S"]) if traffic_per_token
+                         "traffic": (traffic_ratio * alg_bytes_launch) if traffic_ratio
                          else None,
                          "kernel": kname,
                          "algorithmic_bytes_per_launch": alg_bytes_launch},
@@ -536,6 +565,9 @@ def main():
     ap.add_argument("--seq", type=int, default=0, help="override cached positions")
     ap.add_argument("--force-simt", action="store_true",
                     help="time the CUDA-core decode kernel even where tensor cores apply")
+    ap.add_argument("--seq-shards", type=int, default=0,
+                    help="sharded configs: ranks per sequence split (0: as many KV-head "
+                         "shards as divide the ranks, the rest split the sequence)")
     ap.add_argument("--splits", type=int, default=0,
                     help="force this many sequence splits per row (0: planner's choice)")
     args = ap.parse_args()

@@ -1,5 +1,7 @@
 // decode_mma.cu - fused softmax attention over the Q4 cache on the tensor
-// cores (mma.sync), for GQA groups of 4 or 8 query heads per KV head.
+// cores (mma.sync), for any number of query heads per KV head (MHA
+// included): a CTA serves up to 8 query heads of one KV head, with its
+// fragments laid out for 4 or 8.
 //
 // Same work decomposition, page pipeline and merge as the CUDA-core kernel
 // in decode.cu; what changes is how the two contractions of a position
@@ -53,28 +55,31 @@
 namespace eakv {
 namespace {
 
-template <int HD, int GH>
+// RH: query heads a CTA's fragments are laid out for (4 or 8); a CTA
+// serves gh <= RH live heads (the planner's choice), the rest of its rows
+// are zero and their results are discarded.
+template <int HD, int RH>
 struct MCfg {
   static constexpr int NG = HD / 64;                        // groups per position
   static constexpr int KSG = 2;                             // score k-steps (32 dims) per group
-  static constexpr int KMT = GH / 4;                        // score m-tiles (4 heads x 4 digits)
-  static constexpr int VNT = GH == 8 ? 2 : 1;               // P' n-tiles (one per limb)
+  static constexpr int KMT = RH / 4;                        // score m-tiles (4 heads x 4 digits)
+  static constexpr int VNT = RH == 8 ? 2 : 1;               // P' n-tiles (one per limb)
   static constexpr int VMT = 4 * NG;                        // output m-tiles of 16 dims
   static constexpr int NW = 4;                              // warps; each takes 16 positions of a page
   static constexpr int THREADS = NW * 32;
   // CTAs per SM the register budget is cut for (128 registers at 4)
-  static constexpr int MINB = (HD == 128 && GH == 8) ? 3 : 4;
+  static constexpr int MINB = (HD == 128 && RH == 8) ? 3 : 4;
   static constexpr int NIB = kPagePositions * NG * 32;
   static constexpr int PB = kPagePositions * NG * 40;
   static constexpr int NSTAGE = HD == 128 ? 4 : 8;
   static constexpr int STAGE_BYTES = 2 * PB;
   static constexpr int RING = NSTAGE * STAGE_BYTES;
-  static constexpr int MERGE_BYTES = NW * GH * (HD + 2) * 4;
+  static constexpr int MERGE_BYTES = NW * RH * (HD + 2) * 4;
   static constexpr int MAIN = (RING > MERGE_BYTES ? RING : MERGE_BYTES);
-  static constexpr int QOFF = MAIN + 2 * NSTAGE * 8;          // scaled queries [GH][HD]
-  static constexpr int STATOFF = QOFF + GH * HD * 4;           // [GH] max|q|, [GH][NG] sums
-  static constexpr int SMEM = STATOFF + GH * (1 + NG) * 4;
-  static_assert(GH == 4 || GH == 8, "tensor-core path serves 4 or 8 query heads per KV head");
+  static constexpr int QOFF = MAIN + 2 * NSTAGE * 8;          // scaled queries [RH][HD]
+  static constexpr int STATOFF = QOFF + RH * HD * 4;           // [RH] max|q|, [RH][NG] sums
+  static constexpr int SMEM = STATOFF + RH * (1 + NG) * 4;
+  static_assert(RH == 4 || RH == 8, "fragments are laid out for 4 or 8 query heads");
 };
 
 constexpr uint32_t kMagic = 0x64006400u;   // f16x2 (1024, 1024)
@@ -139,10 +144,10 @@ __device__ __forceinline__ int digit(int x, int l) {
   return d;
 }
 
-template <int HD, int GH>
-__global__ void __launch_bounds__(MCfg<HD, GH>::THREADS, MCfg<HD, GH>::MINB)
+template <int HD, int RH>
+__global__ void __launch_bounds__(MCfg<HD, RH>::THREADS, MCfg<HD, RH>::MINB)
 decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ DecodeBatch batch) {
-  using C = MCfg<HD, GH>;
+  using C = MCfg<HD, RH>;
   constexpr int NG = C::NG;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::MAIN);
@@ -151,7 +156,8 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const int G = a.n_q_heads / a.geom.n_heads;
-  const int nhg = G / GH;
+  const int gh = a.cta_heads;   // live query heads of this CTA (<= RH)
+  const int nhg = G / gh;
   const Item it = decode_item(a, batch, nhg);
   const size_t kv_stride = (size_t)a.geom.n_heads * a.geom.n_pages;
   const uint8_t *kpages = batch.base[it.b] + page_index(a.geom, it.layer, 0, it.h, 0) * C::PB;
@@ -181,19 +187,20 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
     for (int i = 0; i < it.npages && i < C::NSTAGE; i++) issue(i);
 
   // ---- per-thread query fragments -----------------------------------------
-  const int qh0 = it.h * G + it.hg * GH;
+  const int qh0 = it.h * G + it.hg * gh;
   const float *qb = a.q + ((size_t)(it.b * a.n_layers + it.lrow) * a.n_q_heads + qh0) * HD;
   // Score rows: row g of m-tile mt is (head h_mine, digit l_row + 2 mt),
   // row g+8 the next digit. With 4 heads, lanes g and g^4 share a head
   // (digits 0,1 and 2,3); with 8, m-tiles 0 and 1 give lane g all four.
-  const int h_mine = (GH == 4) ? (g & 3) : g;
-  const int l_row = (GH == 4) ? 2 * (g >> 2) : 0;
+  const int h_mine = (RH == 4) ? (g & 3) : g;
+  const int l_row = (RH == 4) ? 2 * (g >> 2) : 0;
   const float qscale = rsqrtf((float)HD) * kLog2e;
   // stage the scaled query block; one warp per head computes max|q| and
   // the per-group sums (for the bias term)
-  for (int i = threadIdx.x; i < GH * HD; i += C::THREADS) q_s[i] = qb[i] * qscale;
+  // (heads gh..RH-1 are idle: zero queries, results never written)
+  for (int i = threadIdx.x; i < RH * HD; i += C::THREADS) q_s[i] = i < gh * HD ? qb[i] * qscale : 0.0f;
   __syncthreads();
-  for (int h = warp; h < GH; h += C::NW) {
+  for (int h = warp; h < RH; h += C::NW) {
     float mx = 0.0f;
     for (int d = lane; d < HD; d += 32) mx = fmaxf(mx, fabsf(q_s[h * HD + d]));
 #pragma unroll
@@ -201,7 +208,7 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
       float sm = q_s[h * HD + 64 * gg + lane] + q_s[h * HD + 64 * gg + 32 + lane];
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
-      if (lane == 0) stat_s[GH + h * NG + gg] = sm;
+      if (lane == 0) stat_s[RH + h * NG + gg] = sm;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -250,7 +257,7 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
   float qsum[NG];
 #pragma unroll
   for (int gg = 0; gg < NG; gg++)
-    qsum[gg] = (GH == 4 && l_row) ? 0.0f : stat_s[GH + h_mine * NG + gg];
+    qsum[gg] = (RH == 4 && l_row) ? 0.0f : stat_s[RH + h_mine * NG + gg];
 
   // ---- accumulators -----------------------------------------------------------
   float dv[C::VMT][C::VNT][4];
@@ -272,7 +279,7 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
   // head of each P'/output column this thread holds: n = 2c + e
   int hcol[2];
 #pragma unroll
-  for (int e = 0; e < 2; e++) hcol[e] = (C::VNT == 1) ? ((2 * c + e) % GH) : (2 * c + e);
+  for (int e = 0; e < 2; e++) hcol[e] = (C::VNT == 1) ? ((2 * c + e) % RH) : (2 * c + e);
   const int my_limb = (C::VNT == 1) ? (g >> 2) : 0;
 
   // One 16-position step of a staged page (this warp's quarter of it).
@@ -351,7 +358,7 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
         part *= w_row;
 #pragma unroll
         for (int gg = 0; gg < NG; gg++) part = fmaf(bk[j][gg], qsum[gg], part);
-        if (GH == 4) part += __shfl_xor_sync(0xffffffffu, part, 16);
+        if (RH == 4) part += __shfl_xor_sync(0xffffffffu, part, 16);
         sc[j] = (FULL || tval[j]) ? part : -INFINITY;
       }
     }
@@ -481,13 +488,13 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
     for (int gg = 0; gg < NG; gg++) pbc[e][gg] = __shfl_sync(0xffffffffu, pb[gg], 4 * hcol[e]);
 
   __syncthreads();   // ring no longer read; reuse it for the merge
-  float *mw = reinterpret_cast<float *>(smem);   // [NW][GH]
-  float *lw = mw + C::NW * GH;                    // [NW][GH]
-  float *ow = lw + C::NW * GH;                    // [NW][GH][HD]
-  if (c == 0 && g < GH) {
-    // lane (g, 0) scores head g (g < GH rows carry every head once)
-    mw[warp * GH + h_mine] = m_run;
-    lw[warp * GH + h_mine] = l_run;
+  float *mw = reinterpret_cast<float *>(smem);   // [NW][RH]
+  float *lw = mw + C::NW * RH;                    // [NW][RH]
+  float *ow = lw + C::NW * RH;                    // [NW][RH][HD]
+  if (c == 0 && g < RH) {
+    // lane (g, 0) scores head g (g < RH rows carry every head once)
+    mw[warp * RH + h_mine] = m_run;
+    lw[warp * RH + h_mine] = l_run;
   }
   // after the limb sum, lanes c and c^2 hold the same columns (one limb pair)
   const bool writer = (C::VNT == 1) ? (c < 2) : true;
@@ -501,26 +508,26 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
 #pragma unroll
       for (int e = 0; e < 2; e++) {
         const int h = hcol[e];
-        ow[(warp * GH + h) * HD + dlo] = fmaf(dv[mv][0][e], vs, pbc[e][gg]);
-        ow[(warp * GH + h) * HD + dhi] = fmaf(dv[mv][0][2 + e], vs * (1.0f / 16.0f), pbc[e][gg]);
+        ow[(warp * RH + h) * HD + dlo] = fmaf(dv[mv][0][e], vs, pbc[e][gg]);
+        ow[(warp * RH + h) * HD + dhi] = fmaf(dv[mv][0][2 + e], vs * (1.0f / 16.0f), pbc[e][gg]);
       }
     }
   }
   __syncthreads();
   const size_t row0 = (size_t)(it.b * a.n_layers + it.lrow) * a.n_q_heads + qh0;
-  for (int idx = threadIdx.x; idx < GH * HD; idx += C::THREADS) {
+  for (int idx = threadIdx.x; idx < gh * HD; idx += C::THREADS) {
     const int h = idx / HD, d = idx - h * HD;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < C::NW; w++) M = fmaxf(M, mw[w * GH + h]);
+    for (int w = 0; w < C::NW; w++) M = fmaxf(M, mw[w * RH + h]);
     float O = 0.0f, L = 0.0f;
     if (M != -INFINITY) {
 #pragma unroll
       for (int w = 0; w < C::NW; w++) {
-        const float mwv = mw[w * GH + h];
+        const float mwv = mw[w * RH + h];
         const float f = mwv == -INFINITY ? 0.0f : ex2(mwv - M);
-        O = fmaf(f, ow[(w * GH + h) * HD + d], O);
-        L = fmaf(f, lw[w * GH + h], L);
+        O = fmaf(f, ow[(w * RH + h) * HD + d], O);
+        L = fmaf(f, lw[w * RH + h], L);
       }
     }
     const size_t row = row0 + h;
@@ -538,10 +545,10 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
   }
 }
 
-template <int HD, int GH>
+template <int HD, int RH>
 int launch_one(const DecodeArgs &a, const DecodeBatch &b, int n_blocks, cudaStream_t s) {
-  using C = MCfg<HD, GH>;
-  auto fn = decode_mma_kernel<HD, GH>;
+  using C = MCfg<HD, RH>;
+  auto fn = decode_mma_kernel<HD, RH>;
   static unsigned long long attr_done = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -554,15 +561,15 @@ int launch_one(const DecodeArgs &a, const DecodeBatch &b, int n_blocks, cudaStre
   return check_cuda(cudaGetLastError(), "decode_mma launch");
 }
 
-template <int HD, int GH>
+template <int HD, int RH>
 int resident_one() {
-  using C = MCfg<HD, GH>;
+  using C = MCfg<HD, RH>;
   static int cached = 0;
   if (cached) return cached;
-  cudaFuncSetAttribute(decode_mma_kernel<HD, GH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaFuncSetAttribute(decode_mma_kernel<HD, RH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        C::SMEM);
   int per_sm = 1, dev = 0, sms = 148;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_mma_kernel<HD, GH>, C::THREADS,
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_mma_kernel<HD, RH>, C::THREADS,
                                                 C::SMEM);
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -573,21 +580,27 @@ int resident_one() {
 }  // namespace
 
 int mma_heads_per_cta(int G, int head_dim) {
-  if (head_dim != 64 && head_dim != 128) return 0;
-  if (G % 8 == 0) return 8;
-  if (G % 4 == 0) return 4;
-  return 0;
+  if ((head_dim != 64 && head_dim != 128) || G <= 0) return 0;
+  // every query head of a KV head in one CTA when they fit (the pages are
+  // read once); otherwise the largest divisor of G up to 8
+  for (int gh = G < 8 ? G : 8; gh > 1; gh--)
+    if (G % gh == 0) return gh;
+  return 1;
 }
 
 int mma_resident(int gh, int head_dim) {
-  if (head_dim == 128) return gh == 8 ? resident_one<128, 8>() : resident_one<128, 4>();
-  return gh == 8 ? resident_one<64, 8>() : resident_one<64, 4>();
+  const bool r8 = gh > 4;
+  if (head_dim == 128) return r8 ? resident_one<128, 8>() : resident_one<128, 4>();
+  return r8 ? resident_one<64, 8>() : resident_one<64, 4>();
 }
 
-int mma_launch(int gh, const DecodeArgs &a, const DecodeBatch &b, int n_blocks, cudaStream_t s) {
+int mma_launch(int gh, const DecodeArgs &a0, const DecodeBatch &b, int n_blocks, cudaStream_t s) {
+  DecodeArgs a = a0;
+  a.cta_heads = gh;
+  const bool r8 = gh > 4;
   if (a.head_dim == 128)
-    return gh == 8 ? launch_one<128, 8>(a, b, n_blocks, s) : launch_one<128, 4>(a, b, n_blocks, s);
-  return gh == 8 ? launch_one<64, 8>(a, b, n_blocks, s) : launch_one<64, 4>(a, b, n_blocks, s);
+    return r8 ? launch_one<128, 8>(a, b, n_blocks, s) : launch_one<128, 4>(a, b, n_blocks, s);
+  return r8 ? launch_one<64, 8>(a, b, n_blocks, s) : launch_one<64, 4>(a, b, n_blocks, s);
 }
 
 }  // namespace eakv

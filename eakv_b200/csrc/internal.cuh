@@ -149,6 +149,7 @@ struct DecodeArgs {
                                     // requested, so its wait runs out (tests only)
   // filled by the planner
   int n_splits, split_pages;
+  int cta_heads;                    // tensor-core path: query heads per CTA
   float *part_m, *part_l, *part_o;
 };
 int decode_launch(const DecodeArgs &a, const DecodeBatch &batch, void *workspace,
@@ -157,8 +158,8 @@ size_t decode_workspace_bytes(const DecodeArgs &a, const DecodeBatch &batch);
 int lse_combine_launch(int n_parts, int n_rows, int head_dim, const float *parts,
                        const float *lse, float *out, float *lse_out, cudaStream_t s);
 int *device_status_ptr();   // status word of the current device
-// decode_mma.cu: tensor-core decode for 4 or 8 query heads per KV head
-int mma_heads_per_cta(int G, int head_dim);   // 0 when the shape is not served
+// decode_mma.cu: tensor-core decode, any number of query heads per KV head
+int mma_heads_per_cta(int G, int head_dim);   // 0 when the head_dim is not served
 int mma_resident(int gh, int head_dim);
 int mma_launch(int gh, const DecodeArgs &a, const DecodeBatch &b, int n_blocks, cudaStream_t s);
 extern thread_local int t_force_path;

@@ -18,6 +18,12 @@
 // nibbles) as two 16-byte loads, and stores the 4 packed bytes as one
 // 32-bit word, so a warp moves 4 groups with fully coalesced traffic.
 // HBM-bound: 256 B read + 40 B written per group.
+//
+// The cache keeps, per (layer, KV head), the largest biased exponent of any
+// V scale (the decode kernels scale probabilities by it). A second, small
+// kernel raises that table from the scales just written: 8 B read per V
+// group and one atomicMax per block, so the quantize loop itself carries
+// no bookkeeping.
 #include "internal.cuh"
 
 namespace eakv {
@@ -46,19 +52,18 @@ quantize_kernel(const float *__restrict__ src, uint8_t *__restrict__ dst, PageGe
   const int j = lane & 7;                 // thread within the group
   const long long warps = (long long)gridDim.x * (kThreads / 32);
   const long long warp_id = (long long)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
-  // Largest V-scale exponent this group leader has produced for the
-  // (layer, head) entry v_idx, published to the cache's exponent table when
-  // the entry changes and at the end (one atomic per run of groups instead
-  // of one per group).
-  int v_idx = -1, v_e = 0;
 
-  // Group gih of unit u: the reference quantizes n_tok*gpd consecutive
-  // 64-float groups starting at the unit's first element
-  // (src/cache.c:78,85-88 and :136-142).
-  auto load = [&](long long gi, float (&v)[8]) {
-    if (gi < n_groups) {
-      const long long u = gi / groups_per_unit;
-      const long long gih = gi - u * groups_per_unit;
+  for (long long gb = warp_id * 4; gb < n_groups; gb += warps * 4) {
+    const long long gi = gb + (lane >> 3);
+    const bool valid = gi < n_groups;
+    float v[8];
+    long long u = 0, gih = 0;
+    if (valid) {
+      // Group gih of unit u: the reference quantizes n_tok*gpd consecutive
+      // 64-float groups starting at the unit's first element
+      // (src/cache.c:78,85-88 and :136-142).
+      u = gi / groups_per_unit;
+      gih = gi - u * groups_per_unit;
       const float *x = src + (size_t)u * n_tok * head_dim + (size_t)gih * 64;
       if (kVec) {
         float4 a = *reinterpret_cast<const float4 *>(x + 4 * j);
@@ -76,21 +81,6 @@ quantize_kernel(const float *__restrict__ src, uint8_t *__restrict__ dst, PageGe
 #pragma unroll
       for (int e = 0; e < 8; e++) v[e] = 0.0f;
     }
-  };
-
-  // each iteration loads the next group before it quantizes this one, so
-  // two loads per thread are in flight
-  float nxt[8];
-  load(warp_id * 4 + (lane >> 3), nxt);
-  for (long long gb = warp_id * 4; gb < n_groups; gb += warps * 4) {
-    const long long gi = gb + (lane >> 3);
-    const bool valid = gi < n_groups;
-    float v[8];
-#pragma unroll
-    for (int e = 0; e < 8; e++) v[e] = nxt[e];
-    if (gb + warps * 4 < n_groups) load(gi + warps * 4, nxt);
-    const long long u = valid ? gi / groups_per_unit : 0;
-    const long long gih = gi - u * groups_per_unit;
 
     float mn = v[0], mx = v[0];
 #pragma unroll
@@ -162,23 +152,40 @@ quantize_kernel(const float *__restrict__ src, uint8_t *__restrict__ dst, PageGe
       *reinterpret_cast<uint32_t *>(pp + (size_t)slot * 32 + 4 * j) = word;
       if (j == 0) {
         *reinterpret_cast<float2 *>(pp + g.nib_bytes + (size_t)slot * 8) = make_float2(scale, mn);
-        const int U = unit_base + (int)u;              // (layer * 2 + kv) * heads + head
-        const int lkv = U / g.n_heads;
-        if (lkv & 1) {
-          const int idx = (lkv >> 1) * g.n_heads + (U - lkv * g.n_heads);
-          const int e = (int)((__float_as_uint(scale) >> 23) & 0xFF);
-          if (idx != v_idx) {
-            if (v_idx >= 0) atomicMax(vexp_table(dst, g) + v_idx, v_e);
-            v_idx = idx;
-            v_e = e;
-          } else {
-            v_e = max(v_e, e);
-          }
-        }
       }
     }
   }
-  if (v_idx >= 0) atomicMax(vexp_table(dst, g) + v_idx, v_e);
+}
+
+// Raises the cache's V-scale exponent table over the groups just written:
+// block (x, y) takes chunk x of unit unit_base + y (K units return at once),
+// reduces the biased exponents of its scales and makes one atomicMax.
+__global__ void __launch_bounds__(kThreads)
+vexp_kernel(uint8_t *__restrict__ dst, PageGeom g, int unit_base, int n_tok, int pos0) {
+  const int U = unit_base + (int)blockIdx.y;   // (layer * 2 + kv) * heads + head
+  const int lkv = U / g.n_heads;
+  if (!(lkv & 1)) return;
+  const long long per_unit = (long long)n_tok * g.gpd;
+  int e = 0;
+  for (long long gi = (long long)blockIdx.x * kThreads + threadIdx.x; gi < per_unit;
+       gi += (long long)gridDim.x * kThreads) {
+    const int t = (int)(gi / g.gpd);
+    const int grp = (int)(gi - (long long)t * g.gpd);
+    const int pos = pos0 + t;
+    const int page = pos / kPagePositions;
+    const uint8_t *pp = dst + ((size_t)U * g.n_pages + page) * g.page_bytes;
+    const float scale = reinterpret_cast<const float2 *>(pp + g.nib_bytes)
+                            [(pos - page * kPagePositions) * g.gpd + grp].x;
+    e = max(e, (int)((__float_as_uint(scale) >> 23) & 0xFF));
+  }
+  e = __reduce_max_sync(0xffffffffu, e);
+  __shared__ int wmax[kThreads / 32];
+  if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = e;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kThreads / 32; w++) e = max(e, wmax[w]);
+    atomicMax(vexp_table(dst, g) + (lkv >> 1) * g.n_heads + (U - lkv * g.n_heads), e);
+  }
 }
 
 }  // namespace
@@ -189,26 +196,30 @@ cudaError_t launch_quantize(const PageGeom &g, uint8_t *d_buf, const float *d_sr
   if (g.gpd <= 0 || n_units <= 0 || n_tok <= 0) return cudaSuccess;
   const long long n_groups = (long long)n_units * n_tok * g.gpd;
   long long blocks = (n_groups + 31) / 32;
-  const bool vec = ((uintptr_t)d_src & 15) == 0 && (head_dim & 3) == 0;
-  // one wave of resident blocks: the grid-stride loop gives every block the
-  // same share, so blocks beyond the resident set would run as a second,
-  // mostly idle wave
-  int dev = 0, sms = 148, per_sm = 0;
+  int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  cudaError_t e = vec ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                            &per_sm, quantize_kernel<true>, kThreads, 0)
-                      : cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-                            &per_sm, quantize_kernel<false>, kThreads, 0);
-  if (e != cudaSuccess) return e;
-  const long long cap = (long long)sms * (per_sm > 0 ? per_sm : 1);
+  long long cap = (long long)sms * 8;
   if (blocks > cap) blocks = cap;
-  if (vec)
+  if (((uintptr_t)d_src & 15) == 0 && (head_dim & 3) == 0)
     quantize_kernel<true><<<(int)blocks, kThreads, 0, s>>>(d_src, d_buf, g, unit_base, n_groups,
                                                            n_tok, pos0, head_dim);
   else
     quantize_kernel<false><<<(int)blocks, kThreads, 0, s>>>(d_src, d_buf, g, unit_base, n_groups,
                                                             n_tok, pos0, head_dim);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  // V units in the range: keep the per-(layer, head) max V-scale exponent
+  const int first_v = (unit_base / g.n_heads) | 1;   // first (layer, V) slice at or after
+  if (first_v * g.n_heads >= unit_base + n_units && (unit_base / g.n_heads) % 2 == 0) return cudaSuccess;
+  const long long per_unit = (long long)n_tok * g.gpd;
+  long long chunks = (per_unit + 8LL * kThreads - 1) / (8LL * kThreads);   // ~8 groups a thread
+  if (chunks > 65535) chunks = 65535;
+  for (int y0 = 0; y0 < n_units; y0 += 65535) {
+    const int ny = n_units - y0 < 65535 ? n_units - y0 : 65535;
+    vexp_kernel<<<dim3((unsigned)chunks, (unsigned)ny), kThreads, 0, s>>>(d_buf, g, unit_base + y0,
+                                                                         n_tok, pos0);
+  }
   return cudaGetLastError();
 }
 

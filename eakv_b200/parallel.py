@@ -18,6 +18,8 @@ so a rank's slice can sit at local positions 0.. of its caches.
 torch.distributed is the plumbing (NCCL on GPUs, gloo on CPU for the
 tests); the kernels are the library's.
 """
+import math
+
 import numpy as np
 
 from . import decode_attention_partial, lse_combine
@@ -36,6 +38,27 @@ def seq_shard(seq_len, world, rank, align=PAGE):
     begin = min(seq_len, rank * per)
     end = min(seq_len, begin + per) if rank < world - 1 else seq_len
     return begin, max(begin, end)
+
+
+def shard_layout(world, n_kv_heads, seq_shards=0):
+    """(head_shards, seq_shards) with head_shards * seq_shards == world.
+
+    KV heads are independent (each GPU decodes its heads for every
+    sequence, no exchange), so by default as many head shards as divide
+    both `world` and `n_kv_heads` are used and the remaining factor splits
+    the sequence. `seq_shards` > 0 fixes the split instead; it must divide
+    `world`, and `world // seq_shards` must divide `n_kv_heads`.
+    Rank r belongs to head shard r // seq_shards and sequence slice
+    r % seq_shards."""
+    if world <= 0 or n_kv_heads <= 0:
+        raise ValueError("bad world/heads")
+    if seq_shards <= 0:
+        hs = math.gcd(world, n_kv_heads)
+        return hs, world // hs
+    if world % seq_shards or n_kv_heads % (world // seq_shards):
+        raise ValueError(f"{seq_shards} sequence shards do not fit {world} ranks and "
+                         f"{n_kv_heads} KV heads")
+    return world // seq_shards, seq_shards
 
 
 def merge_partials_np(outs, lses):

@@ -108,3 +108,79 @@ def test_merge_handles_empty_parts():
     np.testing.assert_allclose(out[0], 2.0, rtol=1e-6)        # equal weights of 1 and 3
     np.testing.assert_allclose(out[1], 1.0, rtol=1e-6)        # only part 0 counts
     np.testing.assert_allclose(lse, [np.log(2.0), 1.0], rtol=1e-6)
+
+
+def test_shard_layout():
+    from eakv_b200.parallel import shard_layout
+    assert shard_layout(1, 8) == (1, 1)
+    assert shard_layout(2, 8) == (2, 1)
+    assert shard_layout(8, 8) == (8, 1)
+    assert shard_layout(16, 8) == (8, 2)      # beyond one KV head per rank: split sequences
+    assert shard_layout(6, 4) == (2, 3)
+    assert shard_layout(4, 8, seq_shards=2) == (2, 2)
+    assert shard_layout(8, 8, seq_shards=8) == (1, 8)
+    with pytest.raises(ValueError):
+        shard_layout(4, 8, seq_shards=3)
+    with pytest.raises(ValueError):
+        shard_layout(8, 2, seq_shards=2)      # 4 head shards of 2 KV heads
+
+
+def _worker_2d(rank, world, port, seq_shards, S, result_q):
+    """KV-head shards x sequence split: each rank holds the KV heads of its
+    head shard (with their query heads) over its slice of the positions;
+    ranks of one head shard all-gather and merge over their own group."""
+    import torch
+    import torch.distributed as dist
+    from eakv_b200.parallel import shard_layout
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle import oracle as O
+        L, nq, nkv, hd = 1, 8, 4, 64
+        hs, ss = shard_layout(world, nkv, seq_shards)
+        h_i, s_i = rank // ss, rank % ss
+        groups = [dist.new_group(ranks=[h * ss + k for k in range(ss)]) for h in range(hs)]
+        rng = np.random.default_rng(1)
+        data = rng.standard_normal((L, 2, nkv, S, hd)).astype(np.float32)
+        q = rng.standard_normal((L, nq, hd)).astype(np.float32)
+        kh, qh = nkv // hs, nq // hs
+        mine = np.ascontiguousarray(data[:, :, h_i * kh:(h_i + 1) * kh])
+        qm = np.ascontiguousarray(q[:, h_i * qh:(h_i + 1) * qh])
+        rc = O.RefCache(L, kh, hd, S)
+        rc.load_raw(mine, S)
+        lo, hi = seq_shard(S, ss, s_i)
+        o, s = _partial_oracle(rc, qm[0], 0, qh, kh, lo, hi)
+        part = torch.from_numpy(o.reshape(qh, hd))
+        lse = torch.from_numpy(s)
+        parts = [torch.empty_like(part) for _ in range(ss)]
+        lsel = [torch.empty_like(lse) for _ in range(ss)]
+        dist.all_gather(parts, part, group=groups[h_i])
+        dist.all_gather(lsel, lse, group=groups[h_i])
+        merged, _ = merge_partials_np(np.stack([p.numpy() for p in parts]),
+                                      np.stack([x.numpy() for x in lsel]))
+        full_rc = O.RefCache(L, nkv, hd, S)
+        full_rc.load_raw(data, S)
+        full = full_rc.fused(q[0], 0, nq, nkv).reshape(nq, hd)[h_i * qh:(h_i + 1) * qh]
+        err = np.abs(merged - full)
+        ok = bool(np.all(err <= 1e-4 + 1e-4 * np.abs(full)))
+        result_q.put((rank, ok, float(err.max())))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,seq_shards,S", [(4, 2, 300), (2, 1, 130)])
+def test_head_shards_times_sequence_split_gloo(world, seq_shards, S):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_2d, args=(r, world, port, seq_shards, S, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, ok, err in results:
+        assert ok, f"rank {rank}: max err {err}"
