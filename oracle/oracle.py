@@ -35,6 +35,7 @@ _SFX = "_v4" if AVX512 else ""
 ORACLE_SO = os.path.join(HERE, "_build", f"liboracle{_SFX}.so")
 REF_SO = os.path.join(HERE, "_ref", f"libeakv_ref{_SFX}.so")
 GGML_SCALAR_SO = os.path.join(HERE, "_ref", "ggml_scalar.so")
+GGML_AVX512_SO = os.path.join(HERE, "_ref", "ggml_avx512.so")
 
 _P = ctypes.c_void_p
 _I = ctypes.c_int32
@@ -68,6 +69,10 @@ def olib():
         L.oracle_fused_attention.argtypes = [_P] * 8 + [_I, _I, _I, _I, _I]
         L.q4_validate.argtypes = [_P, _P, _P, _P, _I]
         L.q4_validate.restype = _I
+        L.oracle_ggml_quantize_row.argtypes = [_P, _P, ctypes.c_int64]
+        L.oracle_ggml_dequantize_row.argtypes = [_P, _P, ctypes.c_int64]
+        L.oracle_ggml_vec_dot.argtypes = [ctypes.c_int, _P, ctypes.c_size_t, _P, ctypes.c_size_t,
+                                          _P, ctypes.c_size_t, ctypes.c_int]
         _olib = L
     return _olib
 
@@ -95,6 +100,48 @@ def dequantize(w, s, b):
     olib().q4_dequantize_avx512_f32(ptr(w), ptr(np.ascontiguousarray(s, np.float32)),
                                     ptr(np.ascontiguousarray(b, np.float32)), ptr(out), n)
     return out
+
+
+def _ggml_fns(lib):
+    if lib is None:
+        L = olib()
+        return (L.oracle_ggml_quantize_row, L.oracle_ggml_dequantize_row, L.oracle_ggml_vec_dot)
+    for n in ("eakv_quantize_row", "eakv_dequantize_row"):
+        getattr(lib, n).argtypes = [_P, _P, ctypes.c_int64]
+    lib.eakv_vec_dot_q4_f32.argtypes = [ctypes.c_int, _P, ctypes.c_size_t, _P, ctypes.c_size_t,
+                                        _P, ctypes.c_size_t, ctypes.c_int]
+    return lib.eakv_quantize_row, lib.eakv_dequantize_row, lib.eakv_vec_dot_q4_f32
+
+
+def ggml_quantize(x, lib=None):
+    """ggml q4_1_eakv from_float (src/ggml_type.c:21-93, AVX-512 build):
+    f32[n*64] -> u8[n][40] blocks {qs[32], d, m}. `lib`: a CDLL exporting
+    the reference names (the compiled reference, or the CUDA library);
+    None: the restatement."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    n = x.size // 64
+    out = np.zeros(n * 40, np.uint8)
+    _ggml_fns(lib)[0](ptr(x), ptr(out), n * 64)
+    return out.reshape(n, 40)
+
+
+def ggml_dequantize(blocks, lib=None):
+    blocks = np.ascontiguousarray(blocks, np.uint8).reshape(-1)
+    n = blocks.size // 40
+    out = np.zeros(n * 64, np.float32)
+    _ggml_fns(lib)[1](ptr(blocks), ptr(out), n * 64)
+    return out
+
+
+def ggml_vec_dot(blocks, y, lib=None):
+    """Row r of `blocks` (u8[nrc][nb*40]) dotted with row r of y
+    (f32[nrc][nb*64]) -> f32[nrc] (ggml_type.c:138-242, nrc rows)."""
+    blocks = np.ascontiguousarray(blocks, np.uint8)
+    y = np.ascontiguousarray(y, np.float32)
+    nrc, n = y.shape
+    s = np.zeros(nrc, np.float32)
+    _ggml_fns(lib)[2](n, ptr(s), 4, ptr(blocks), blocks.shape[1], ptr(y), n * 4, nrc)
+    return s
 
 
 class RefCache:

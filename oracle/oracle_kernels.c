@@ -484,3 +484,107 @@ HOT void oracle_fused_attention(const float *q_vecs, const uint8_t *k_packed,
                         v_biases, all_out, seq_len, n_q_heads, n_kv_heads,
                         groups_per_head, head_dim);
 }
+
+/* ---------------------------------------------------------------------
+ * ggml block type q4_1_eakv: src/ggml_type.c:21-242 (include/eakv_ggml.h),
+ * the AVX-512 build, which is the path the reference ships for x86 ("all
+ * hot paths use AVX-512", ggml_type.c:7). 40-byte blocks {qs[32], d, m},
+ * lo nibble of qs[k] = element k, hi nibble = element k+32.
+ *
+ * Restated with the instruction semantics of that build, lane by lane:
+ *   MINPS(a, b) = a < b ? a : b and MAXPS(a, b) = a > b ? a : b (a NaN or
+ *   two zeros give the second operand); _mm512_reduce_min/max_ps is the
+ *   tree  op(hi256, lo256) -> op(hi128, lo128) -> op(v, v[i^2]) ->
+ *   op(v, v[i^1]), lane 0; _mm512_reduce_add_ps is reduce_add16 above;
+ *   cvttps truncates and gives INT32_MIN for NaN; cvtepi32_epi8 keeps the
+ *   low byte.
+ * ------------------------------------------------------------------- */
+static inline float minps(float a, float b) { return a < b ? a : b; }
+static inline float maxps(float a, float b) { return a > b ? a : b; }
+
+static inline float reduce_minmax16(const float *v, int is_max) {
+    float t3[8], t6[4], t8[4];
+    for (int i = 0; i < 8; i++) t3[i] = is_max ? maxps(v[i + 8], v[i]) : minps(v[i + 8], v[i]);
+    for (int i = 0; i < 4; i++) t6[i] = is_max ? maxps(t3[i + 4], t3[i]) : minps(t3[i + 4], t3[i]);
+    for (int i = 0; i < 4; i++) t8[i] = is_max ? maxps(t6[i], t6[i ^ 2]) : minps(t6[i], t6[i ^ 2]);
+    return is_max ? maxps(t8[0], t8[1]) : minps(t8[0], t8[1]);
+}
+
+static inline int32_t cvtt(float v) {
+    if (!(v >= -2147483648.0f && v < 2147483648.0f)) return INT32_MIN;
+    return (int32_t)v;
+}
+
+/* ggml_type.c:21-93 (from_float). */
+void oracle_ggml_quantize_row(const float *src, void *dst, int64_t k) {
+    uint8_t *out = (uint8_t *)dst;
+    const int64_t nb = k / 64;
+    for (int64_t i = 0; i < nb; i++) {
+        const float *x = src + i * 64;
+        uint8_t *blk = out + i * 40;
+        float vmin[16], vmax[16];
+        for (int l = 0; l < 16; l++) vmin[l] = vmax[l] = x[l];
+        for (int j = 16; j < 64; j += 16)
+            for (int l = 0; l < 16; l++) {
+                vmin[l] = minps(vmin[l], x[j + l]);
+                vmax[l] = maxps(vmax[l], x[j + l]);
+            }
+        const float mn = reduce_minmax16(vmin, 0), mx = reduce_minmax16(vmax, 1);
+        const float range = mx - mn;
+        const float d = range / 15.0f;
+        const float id = range > 0.0f ? 15.0f / range : 0.0f;
+        memcpy(blk + 32, &d, 4);
+        memcpy(blk + 36, &mn, 4);
+        for (int c = 0; c < 2; c++)
+            for (int l = 0; l < 16; l++) {
+                float lo_f = (x[c * 16 + l] - mn) * id;
+                float hi_f = (x[c * 16 + l + 32] - mn) * id;
+                lo_f = minps(15.0f, maxps(0.0f, lo_f + 0.5f));
+                hi_f = minps(15.0f, maxps(0.0f, hi_f + 0.5f));
+                const uint32_t packed = (uint32_t)cvtt(lo_f) | ((uint32_t)cvtt(hi_f) << 4);
+                blk[c * 16 + l] = (uint8_t)(packed & 0xFF);
+            }
+    }
+}
+
+/* ggml_type.c:99-129 (to_float): fmadd(nibble, d, m). */
+void oracle_ggml_dequantize_row(const void *src, float *dst, int64_t k) {
+    const uint8_t *in = (const uint8_t *)src;
+    const int64_t nb = k / 64;
+    for (int64_t i = 0; i < nb; i++) {
+        const uint8_t *blk = in + i * 40;
+        float d, m;
+        memcpy(&d, blk + 32, 4);
+        memcpy(&m, blk + 36, 4);
+        for (int j = 0; j < 32; j++) {
+            dst[i * 64 + j] = fmaf((float)(blk[j] & 15), d, m);
+            dst[i * 64 + j + 32] = fmaf((float)(blk[j] >> 4), d, m);
+        }
+    }
+}
+
+/* ggml_type.c:138-242 (vec_dot, nrc rows): 16 fma lanes, per block
+ * lo(c=0), hi(c=0), lo(c=1), hi(c=1), then the halving-tree sum. */
+void oracle_ggml_vec_dot(int n, float *s, size_t bs, const void *vx, size_t bx,
+                         const void *vy, size_t by, int nrc) {
+    const int nb = n / 64;
+    for (int r = 0; r < nrc; r++) {
+        const uint8_t *blocks = (const uint8_t *)vx + (size_t)r * bx;
+        const float *y = (const float *)((const char *)vy + (size_t)r * by);
+        float acc[16] = {0};
+        for (int i = 0; i < nb; i++) {
+            const uint8_t *blk = blocks + (size_t)i * 40;
+            float d, m;
+            memcpy(&d, blk + 32, 4);
+            memcpy(&m, blk + 36, 4);
+            for (int c = 0; c < 2; c++)
+                for (int l = 0; l < 16; l++) {
+                    const uint8_t raw = blk[c * 16 + l];
+                    acc[l] = fmaf(fmaf((float)(raw & 15), d, m), y[c * 16 + l], acc[l]);
+                    acc[l] = fmaf(fmaf((float)(raw >> 4), d, m), y[c * 16 + 32 + l], acc[l]);
+                }
+            y += 64;
+        }
+        *(float *)((char *)s + (size_t)r * bs) = reduce_add16(acc);
+    }
+}

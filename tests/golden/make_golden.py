@@ -19,6 +19,9 @@ Outputs:
                  the packed nibbles / scales / biases read back from it
   attn_<name>.npz  seeded K/V/queries, reference scores, softmax weights,
                  reference V-sum output and two-pass fused attention output
+  ggml.npz       q4_1_eakv ggml blocks, dequantized values and vec_dot results of
+                 the reference's src/ggml_type.c built with AVX-512
+                 (oracle/_ref/ggml_avx512.so)
 """
 import ctypes
 import os
@@ -183,11 +186,35 @@ def make_attention(R):
         print(f"attn_{name}.npz: L={L} nq={nq} nkv={nkv} hd={hd} S={S} max={maxS}")
 
 
+def make_ggml(rng):
+    """q4_1_eakv ggml type (src/ggml_type.c) from the reference's AVX-512
+    build (oracle/_ref/ggml_avx512.so); the restatement must agree."""
+    G = ctypes.CDLL(O.GGML_AVX512_SO)
+    e = edge_groups(rng)
+    specials = rng.choice(np.array([0.0, -0.0, 1.0, -1.0, np.nan, np.inf, -np.inf, 1e-40, -1e-40,
+                                    3e38, -3e38], np.float32), (64, 64))
+    rnd = (rng.standard_normal((256, 64)) * np.exp(rng.uniform(-30, 30, (256, 1)))).astype(np.float32)
+    x = np.concatenate([e, specials, rnd]).astype(np.float32)
+    blocks = O.ggml_quantize(x, G)
+    assert np.array_equal(blocks, O.ggml_quantize(x)), "restated from_float differs"
+    deq = O.ggml_dequantize(blocks, G)
+    assert np.array_equal(deq.view(np.uint32), O.ggml_dequantize(blocks).view(np.uint32))
+    # vec_dot: 6 rows of 4 blocks (256 elements) against random queries
+    vx = blocks[-24:].reshape(6, 4 * 40)
+    vy = rng.standard_normal((6, 256)).astype(np.float32)
+    dot = O.ggml_vec_dot(vx, vy, G)
+    assert np.array_equal(dot.view(np.uint32), O.ggml_vec_dot(vx, vy).view(np.uint32))
+    np.savez_compressed(os.path.join(OUT, "ggml.npz"), x=x, blocks=blocks, deq=deq, vx=vx, vy=vy,
+                        dot=dot)
+    print(f"ggml.npz: {x.shape[0]} blocks, vec_dot {vx.shape[0]} rows")
+
+
 def main():
     R = O.rlib()
     rng = np.random.default_rng(2026)
     make_quantize(rng, R)
     make_attention(R)
+    make_ggml(np.random.default_rng(2027))
 
 
 if __name__ == "__main__":
