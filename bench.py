@@ -134,11 +134,12 @@ class ClockSampler:
             return None
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        pw = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows)}
+                "power_w": statistics.median(pw) if pw else None, "samples": len(rows)}
 
 
 # ---------------------------------------------------------------------------
@@ -551,12 +552,92 @@ def run_b200(args, cfg, world, rank, local):
     return result
 
 
+def run_ggml(args, world, rank, local):
+    """The q4_1_eakv ggml block type (SURVEY next row 1): from_float,
+    to_float and vec_dot on device buffers, one JSON line each, with the
+    reference's AVX-512 code (or its restatement) timed on one host thread
+    on a bounded sample. HBM-bound; 1 GiB of f32 per pass (> L2)."""
+    import ctypes
+    import torch
+    import eakv_b200 as E
+    from oracle import oracle as O
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    E.set_device(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    sh = stream.cuda_stream
+    nb = 1 << 22                                   # 4.2 M blocks: 1 GiB of f32, 168 MB of blocks
+    k = nb * 64
+    x = torch.randn(k, device=dev)
+    blocks = torch.empty(nb * 40, dtype=torch.uint8, device=dev)
+    out = torch.empty(k, device=dev)
+    row = 128                                      # vec_dot: rows of one head_dim
+    nrc = k // row
+    y = torch.randn(k, device=dev)
+    s = torch.empty(nrc, device=dev)
+    ops = {
+        "from_float": (lambda: E.ggml_quantize_row_device(x, blocks, k, sh), nb * (256 + 40)),
+        "to_float": (lambda: E.ggml_dequantize_row_device(blocks, out, k, sh), nb * (40 + 256)),
+        "vec_dot": (lambda: E.ggml_vec_dot_device(row, s, 4, blocks, row // 64 * 40, y, row * 4,
+                                                   nrc, sh), nb * (40 + 256) + nrc * 4),
+    }
+    peak, peak_kind = measured_peak()
+    have_ref = os.path.exists(O.GGML_AVX512_SO)
+    H = ctypes.CDLL(O.GGML_AVX512_SO) if have_ref else None
+    hx = np.random.default_rng(0).standard_normal(1 << 20).astype(np.float32)   # 16384 blocks
+    hb = O.ggml_quantize(hx, H)
+    hy = np.random.default_rng(1).standard_normal(hx.size).astype(np.float32)
+    host = {
+        "from_float": lambda: O.ggml_quantize(hx, H),
+        "to_float": lambda: O.ggml_dequantize(hb, H),
+        "vec_dot": lambda: O.ggml_vec_dot(hb.reshape(-1, 80), hy.reshape(-1, 128), H),
+    }
+    for name, (fn, nbytes) in ops.items():
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        evs[0].record(stream)
+        for i in range(args.steps):
+            fn()
+            evs[i + 1].record(stream)
+        torch.cuda.synchronize()
+        ms = evs[0].elapsed_time(evs[-1]) / args.steps
+        gbs = nbytes / (ms / 1e3) / 1e9
+        t0, reps = time.time(), 0
+        while time.time() - t0 < args.cpu_seconds / 3:
+            host[name]()
+            reps += 1
+        cpu_gbs = reps * (hx.size // 64) * (nbytes / nb) / (time.time() - t0) / 1e9
+        print(json.dumps({
+            "metric": f"q4_1_eakv ggml {name} GB/s (HBM bytes moved)", "value": gbs,
+            "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (torch.randn)",
+            "config": {"workload": f"ggml {name}: {nb} blocks of 64 (1 GiB f32)"
+                                   + (f", rows of {row}" if name == "vec_dot" else ""),
+                       "l2": "inputs larger than L2, no flush"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                         "frac": gbs / peak, "peak_source": f"{peak_kind} hbm_gbs",
+                         "traffic": None, "algorithmic_bytes_per_launch": nbytes},
+            "cpu_baseline": {"value": cpu_gbs, "unit": "GB/s", "cores": 1,
+                             "kind": "reference" if have_ref else "port",
+                             "sample": f"{hx.size // 64} blocks, {reps} passes"},
+            "gpu_launches": args.steps,
+        }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", type=int, default=4, choices=sorted(CONFIGS))
+    ap.add_argument("--op", default="decode", choices=["decode", "ggml"],
+                    help="ggml: time the q4_1_eakv ggml block type kernels instead")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
@@ -582,7 +663,9 @@ def main():
         cfg["workload"] += f" (seq_len overridden to {args.seq})"
     world, rank, local = dist_setup(args.gpus)
     try:
-        if args.impl == "reference":
+        if args.op == "ggml":
+            run_ggml(args, world, rank, local)
+        elif args.impl == "reference":
             run_reference(args, cfg, world, rank)
         else:
             run_b200(args, cfg, world, rank, local)

@@ -65,7 +65,8 @@ struct MCfg {
   static constexpr int KMT = RH / 4;                        // score m-tiles (4 heads x 4 digits)
   static constexpr int VNT = RH == 8 ? 2 : 1;               // P' n-tiles (one per limb)
   static constexpr int VMT = 4 * NG;                        // output m-tiles of 16 dims
-  static constexpr int NW = 4;                              // warps; each takes 16 positions of a page
+  static constexpr int NW = 4;                              // warps
+  static constexpr int WPP = 2;                             // warps per page
   static constexpr int THREADS = NW * 32;
   // CTAs per SM the register budget is cut for (128 registers at 4)
   static constexpr int MINB = (HD == 128 && RH == 8) ? 3 : 4;
@@ -80,6 +81,7 @@ struct MCfg {
   static constexpr int STATOFF = QOFF + RH * HD * 4;           // [RH] max|q|, [RH][NG] sums
   static constexpr int SMEM = STATOFF + RH * (1 + NG) * 4;
   static_assert(RH == 4 || RH == 8, "fragments are laid out for 4 or 8 query heads");
+  static_assert(NW % WPP == 0 && kPagePositions % (16 * WPP) == 0, "page split");
 };
 
 constexpr uint32_t kMagic = 0x64006400u;   // f16x2 (1024, 1024)
@@ -284,10 +286,9 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
 
   // One 16-position step of a staged page (this warp's quarter of it).
   // FULL: every position of the page is attended (no per-position masks).
-  auto page_body = [&](auto full_tag, const uint8_t *ks_, int page_pos0) {
+  auto page_body = [&](auto full_tag, const uint8_t *ks_, int page_pos0, int p0) {
     constexpr bool FULL = decltype(full_tag)::value;
     const uint8_t *vs_ = ks_ + C::PB;
-    const int p0 = 16 * warp;                         // first position of this warp's step
 
     // positions of this thread's score/probability slots: 2c, 2c+1, 2c+8, 2c+9
     int tpos[4];
@@ -439,8 +440,12 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
     }
   };
 
+  // WPP warps share a page, each taking 64 / WPP positions as 16-position
+  // steps; the NW / WPP warp groups take pages in turn, so the per-page
+  // costs (wait, release, loop) are paid once per 64 / WPP positions
   bool ok = true;
-  for (int i = 0; i < it.npages; i++) {
+  const int wgrp = warp / C::WPP, wsub = warp % C::WPP;
+  for (int i = wgrp; i < it.npages; i += C::NW / C::WPP) {
     const int st = i % C::NSTAGE;
     if (!ok || !mbar_wait(smem_u32(&bars[st]), (i / C::NSTAGE) & 1, a.wait_budget)) {
       atomicOr(a.status, kStatusWaitTimeout);
@@ -450,13 +455,18 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
     const uint8_t *ks_ = smem + st * C::STAGE_BYTES;
     const int page_pos0 = (it.pg0 + i) * kPagePositions;
     const bool full = page_pos0 >= it.r0 && page_pos0 + kPagePositions <= it.r1;
-    if (full)
-      page_body(std::true_type{}, ks_, page_pos0);
-    else
-      page_body(std::false_type{}, ks_, page_pos0);
+#pragma unroll 1
+    for (int s2 = 0; s2 < kPagePositions / (16 * C::WPP); s2++) {
+      const int p0 = (kPagePositions / C::WPP) * wsub + 16 * s2;
+      if (full)
+        page_body(std::true_type{}, ks_, page_pos0, p0);
+      else
+        page_body(std::false_type{}, ks_, page_pos0, p0);
+    }
     __syncwarp();
-    // the last warp to finish with this stage refills it with page i+NSTAGE
-    if (lane == 0 && stage_release_last(reinterpret_cast<int *>(&bars[C::NSTAGE]) + st, C::NW) &&
+    // the last warp of the group to finish with this stage refills it with
+    // page i+NSTAGE
+    if (lane == 0 && stage_release_last(reinterpret_cast<int *>(&bars[C::NSTAGE]) + st, C::WPP) &&
         i + C::NSTAGE < it.npages)
       issue(i + C::NSTAGE);
   }
