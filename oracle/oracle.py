@@ -299,3 +299,57 @@ def rlib():
         L.eakv_cache_seq_len.argtypes = [_P]
         _rlib = L
     return _rlib
+
+
+# ---------------------------------------------------------------------------
+# llama.cpp sequence state (reference src/llama_bridge.c:19-288)
+
+REF_LLAMA_SO = os.path.join(HERE, "_ref", "libeakv_ref_llama.so")
+FP16_STUB_SO = os.path.join(HERE, "_build", "fp16_stub.so")
+
+
+def llama_state(k, v, v_trans, seq_ids=None, k_type=1, v_size_el=2):
+    """Bytes of a llama.cpp sequence state in the layout the reference
+    bridge parses: k, v f16 [n_layers][cells][n_embd]; v_trans stores each
+    V layer as columns [n_embd][cells]."""
+    k = np.ascontiguousarray(k, np.float16)
+    v = np.ascontiguousarray(v, np.float16)
+    L, cells, embd = k.shape
+    out = [np.array([1, cells], np.uint32).tobytes()]
+    for t in range(cells):
+        ids = [0] if seq_ids is None else seq_ids[t]
+        out.append(np.array([t], np.int32).tobytes())
+        out.append(np.array([len(ids)], np.uint32).tobytes())
+        out.append(np.array(ids, np.int32).tobytes())
+    out.append(np.array([1 if v_trans else 0, L], np.uint32).tobytes())
+    for l in range(L):
+        out.append(np.array([k_type], np.int32).tobytes())
+        out.append(np.array([embd * 2], np.uint64).tobytes())
+        out.append(k[l].tobytes())
+    for l in range(L):
+        out.append(np.array([k_type], np.int32).tobytes())
+        if v_trans:
+            out.append(np.array([v_size_el, embd], np.uint32).tobytes())
+            out.append(np.ascontiguousarray(v[l].T).tobytes())
+        else:
+            out.append(np.array([embd * 2], np.uint64).tobytes())
+            out.append(v[l].tobytes())
+    return b"".join(out)
+
+
+def llama_import(k, v, n_kv_heads, head_dim, max_seq_len, cache=None, start_pos=0):
+    """The bridge's arithmetic restated: f16 -> f32, [pos][head][dim] ->
+    [head][pos][dim], eakv_cache_append per (layer, K/V), then advance
+    (llama_bridge.c:74-160 / :215-283). Returns the RefCache."""
+    k = np.asarray(k, np.float16)
+    v = np.asarray(v, np.float16)
+    L, cells, embd = k.shape
+    if cache is None:
+        cache = RefCache(L, n_kv_heads, head_dim, max_seq_len)
+    new = cells - start_pos
+    for kv, src in ((0, k), (1, v)):
+        for l in range(L):
+            x = src[l, start_pos:].astype(np.float32).reshape(new, n_kv_heads, head_dim)
+            cache.append(np.ascontiguousarray(x.transpose(1, 0, 2)), l, kv, new)
+    cache.advance(new)
+    return cache

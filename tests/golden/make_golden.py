@@ -22,6 +22,9 @@ Outputs:
   ggml.npz       q4_1_eakv ggml blocks, dequantized values and vec_dot results of
                  the reference's src/ggml_type.c built with AVX-512
                  (oracle/_ref/ggml_avx512.so)
+  llama.npz      llama.cpp sequence states (f16 rows / transposed V, a two-step
+                 append) and the .eakv files the reference's src/llama_bridge.c
+                 makes of them (oracle/_ref/libeakv_ref_llama.so)
 """
 import ctypes
 import os
@@ -209,12 +212,77 @@ def make_ggml(rng):
     print(f"ggml.npz: {x.shape[0]} blocks, vec_dot {vx.shape[0]} rows")
 
 
+# (name, n_layers, n_kv_heads, head_dim, cells, v_trans, first import cells)
+LLAMA_CONFIGS = [
+    ("rows", 2, 2, 64, 70, 0, 70),
+    ("vtrans", 1, 2, 128, 65, 1, 65),
+    ("append_vtrans", 1, 2, 64, 100, 1, 40),   # 40 cells, then cells 40..99 appended
+]
+
+
+def make_llama(rng):
+    """llama.cpp state import (src/llama_bridge.c) by the reference's own
+    bridge (oracle/_ref/libeakv_ref_llama.so); files saved with the
+    reference's eakv_cache_save (cells == max_seq_len, so they are dense)."""
+    R = ctypes.CDLL(O.REF_LLAMA_SO)
+    R.eakv_from_llama_state.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int,
+                                        ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                        ctypes.POINTER(ctypes.c_void_p)]
+    R.eakv_from_llama_state_append.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t,
+                                               ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                               ctypes.c_int]
+    R.eakv_cache_save.argtypes = [ctypes.c_void_p, ctypes.c_char_p]
+    R.eakv_cache_free.argtypes = [ctypes.c_void_p]
+    out = {}
+    for name, L, H, hd, cells, vt, first in LLAMA_CONFIGS:
+        embd = H * hd
+        k = (rng.standard_normal((L, cells, embd)) * 3).astype(np.float16)
+        v = rng.standard_normal((L, cells, embd)).astype(np.float16)
+        k[0, 0, :4] = [np.inf, -np.inf, 0.0, -0.0]
+        v[0, 1, 5] = np.nan
+        full = O.llama_state(k, v, vt)
+        part = O.llama_state(k[:, :first], v[:, :first], vt)
+        buf = np.frombuffer(part, np.uint8)
+        c = ctypes.c_void_p()
+        assert R.eakv_from_llama_state(buf.ctypes.data, buf.size, L, H, hd, cells,
+                                       ctypes.byref(c)) == 0
+        if first < cells:
+            fb = np.frombuffer(full, np.uint8)
+            assert R.eakv_from_llama_state_append(c, fb.ctypes.data, fb.size, L, H, hd, first) == 0
+        with tempfile.TemporaryDirectory() as td:
+            p = os.path.join(td, "x.eakv")
+            assert R.eakv_cache_save(c, p.encode()) == 0
+            raw = open(p, "rb").read()
+        R.eakv_cache_free(c)
+        # the restated bridge gives the same blocks
+        rc = O.llama_import(k[:, :first], v[:, :first], H, hd, cells)
+        if first < cells:
+            O.llama_import(k, v, H, hd, cells, cache=rc, start_pos=first)
+        _, blocks = parse_eakv(raw)
+        n = rc.seq_len * rc.gpd
+        for lkv, (w, s_, b) in enumerate(blocks):
+            for h in range(H):
+                sl = slice(h * n, (h + 1) * n)
+                g0 = h * rc.gph
+                assert np.array_equal(w[sl], rc.w[lkv, g0:g0 + n])
+                assert np.array_equal(s_[sl].view(np.uint32), rc.s[lkv, g0:g0 + n].view(np.uint32))
+                assert np.array_equal(b[sl].view(np.uint32), rc.b[lkv, g0:g0 + n].view(np.uint32))
+        out[f"{name}_state"] = np.frombuffer(full, np.uint8)
+        if first < cells:
+            out[f"{name}_first"] = np.frombuffer(part, np.uint8)
+        out[f"{name}_file"] = np.frombuffer(raw, np.uint8)
+        out[f"{name}_shape"] = np.array([L, H, hd, cells, vt, first], np.int32)
+        print(f"llama {name}: L={L} H={H} hd={hd} cells={cells} v_trans={vt} first={first}")
+    np.savez_compressed(os.path.join(OUT, "llama.npz"), **out)
+
+
 def main():
     R = O.rlib()
     rng = np.random.default_rng(2026)
     make_quantize(rng, R)
     make_attention(R)
     make_ggml(np.random.default_rng(2027))
+    make_llama(np.random.default_rng(2028))
 
 
 if __name__ == "__main__":
