@@ -31,8 +31,8 @@ _P = _c.c_void_p
 _I = _c.c_int
 _F = _c.c_float
 
-# name -> (restype, argtypes); every symbol declared in include/eakv.h and
-# include/eakv_cuda.h.
+# name -> (restype, argtypes); every symbol declared in the headers of
+# include/.
 SIGNATURES = {
     # eakv.h
     "eakv_cache_create": (_P, [_I, _I, _I, _I]),
@@ -79,6 +79,20 @@ SIGNATURES = {
     "eakv_test_force_splits": (_I, [_I]),
     "eakv_test_force_path": (_I, [_I]),
     "eakv_test_stall": (_I, [_I, ctypes.c_uint]),
+    "eakv_cache_validate": (_I, [_P, _P]),
+    "eakv_cache_dequantize_device": (_I, [_P, _I, _I, _I, _I, _P, _P]),
+    "eakv_cache_dequantize": (_I, [_P, _I, _I, _I, _I, _P]),
+    # eakv_ggml.h
+    "eakv_quantize_row": (None, [_P, _P, _c.c_int64]),
+    "eakv_dequantize_row": (None, [_P, _P, _c.c_int64]),
+    "eakv_vec_dot_q4_f32": (None, [_I, _P, _c.c_size_t, _P, _c.c_size_t, _P, _c.c_size_t, _I]),
+    # eakv_llama.h
+    "eakv_from_llama_state": (_I, [_P, _c.c_size_t, _I, _I, _I, _I, _c.POINTER(_P)]),
+    "eakv_from_llama_state_append": (_I, [_P, _P, _c.c_size_t, _I, _I, _I, _I]),
+    "eakv_ggml_quantize_row_device": (_I, [_P, _P, _c.c_int64, _P]),
+    "eakv_ggml_dequantize_row_device": (_I, [_P, _P, _c.c_int64, _P]),
+    "eakv_ggml_vec_dot_device": (_I, [_I, _P, _c.c_size_t, _P, _c.c_size_t, _P, _c.c_size_t, _I,
+                                      _P]),
 }
 
 _lib = None
@@ -172,6 +186,43 @@ class Cache:
         out = ctypes.c_void_p()
         _check(lib().eakv_cache_load(os.fsencode(path), ctypes.byref(out)), "eakv_cache_load")
         return cls(_handle=out.value)
+
+    @classmethod
+    def from_llama_state(cls, state, n_layers, n_kv_heads, head_dim, max_seq_len):
+        """eakv_from_llama_state on a host bytes object (a llama.cpp
+        sequence state); raises EakvError with the reference's code."""
+        buf = np.frombuffer(state, np.uint8)
+        out = ctypes.c_void_p()
+        _check(lib().eakv_from_llama_state(_ptr(buf), buf.size, n_layers, n_kv_heads, head_dim,
+                                           max_seq_len, ctypes.byref(out)),
+               "eakv_from_llama_state")
+        return cls(_handle=out.value)
+
+    def append_llama_state(self, state, n_layers, n_kv_heads, head_dim, start_pos):
+        """eakv_from_llama_state_append; returns the reference's code."""
+        buf = np.frombuffer(state, np.uint8)
+        return lib().eakv_from_llama_state_append(self.h, _ptr(buf), buf.size, n_layers,
+                                                  n_kv_heads, head_dim, start_pos)
+
+    # --- inspection ----------------------------------------------------------------
+    def validate(self):
+        """eakv_cache_validate: int32[n_layers*2] codes (0 ok, 1 NaN scale,
+        2 NaN bias, 3 negative scale), index layer*2 + kv."""
+        codes = np.zeros(self.n_layers * 2, np.int32)
+        _check(lib().eakv_cache_validate(self.h, _ptr(codes)), "eakv_cache_validate")
+        return codes
+
+    def dequantize(self, layer, kv_idx, pos_begin, pos_end):
+        """f32[n_kv_heads][pos_end - pos_begin][head_dim] on the host."""
+        out = np.zeros((self.n_heads, pos_end - pos_begin, self.head_dim), np.float32)
+        _check(lib().eakv_cache_dequantize(self.h, layer, kv_idx, pos_begin, pos_end, _ptr(out)),
+               "eakv_cache_dequantize")
+        return out
+
+    def dequantize_device(self, layer, kv_idx, pos_begin, pos_end, d_out, stream=None):
+        return _check(lib().eakv_cache_dequantize_device(self.h, layer, kv_idx, pos_begin,
+                                                         pos_end, _ptr(d_out), stream),
+                      "eakv_cache_dequantize_device")
 
     # --- info ----------------------------------------------------------------
     @property
@@ -336,3 +387,20 @@ def test_stall(page, wait_budget=0):
     """Failure-detection aid: decode kernels never request `page` of a work
     item (page < 0: off) and give up each wait after `wait_budget` polls."""
     lib().eakv_test_stall(int(page), int(wait_budget))
+
+
+# --- q4_1_eakv ggml block type on device buffers (include/eakv_ggml.h) ------------
+def ggml_quantize_row_device(d_src, d_dst, k, stream=None):
+    return _check(lib().eakv_ggml_quantize_row_device(_ptr(d_src), _ptr(d_dst), int(k),
+                                                      stream), "ggml_quantize_row_device")
+
+
+def ggml_dequantize_row_device(d_src, d_dst, k, stream=None):
+    return _check(lib().eakv_ggml_dequantize_row_device(_ptr(d_src), _ptr(d_dst), int(k),
+                                                        stream), "ggml_dequantize_row_device")
+
+
+def ggml_vec_dot_device(n, d_s, bs, d_vx, bx, d_vy, by, nrc, stream=None):
+    return _check(lib().eakv_ggml_vec_dot_device(int(n), _ptr(d_s), bs, _ptr(d_vx), bx,
+                                                 _ptr(d_vy), by, int(nrc), stream),
+                  "ggml_vec_dot_device")

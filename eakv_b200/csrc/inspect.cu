@@ -1,0 +1,170 @@
+// inspect.cu - checks and read-back of a resident cache: device validate
+// (reference kernels/validate.ea:14-71 as the CLI runs it, src/cli.c:39-98)
+// and dequantize (reference kernels/dequantize_avx512.ea:10-89).
+//
+// validate: per (layer, K/V), the reference's q4_validate scans the groups
+// in its dense order ([head][position][group], positions < seq_len) and
+// returns at the first group that has a NaN scale (1), a NaN bias (2) or a
+// scale below zero (3), checked in that order. Here every group is checked
+// in parallel; a failing group offers the key index*4 + code to an
+// atomicMin per (layer, K/V), so the smallest key is the reference's first
+// failure and its low two bits its code. Only the (scale, bias) pairs are
+// read: 8 of every 40 bytes of the pages.
+//
+// dequantize: value = fma(nibble, scale, bias) for the lo (element k) and
+// hi (element k+32) nibble of byte k of a group, the reference's f32x16
+// fma, so the values equal the reference's bit for bit.
+#include "internal.cuh"
+
+namespace eakv {
+namespace {
+
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ bool is_nan_bits(float v) {
+  const int b = __float_as_int(v);   // validate.ea:51-62: > 0x7F800000, or in (-0x800000, 0)
+  return b > 2139095040 || (b < 0 && b > -8388608);
+}
+
+__global__ void __launch_bounds__(kThreads)
+validate_kernel(const uint8_t *__restrict__ buf, PageGeom g, int seq_len,
+                unsigned long long *__restrict__ keys) {
+  const int lkv = blockIdx.y;   // layer * 2 + kv
+  const long long per_head = (long long)seq_len * g.gpd;
+  const long long n = per_head * g.n_heads;
+  unsigned long long best = ~0ull;
+  for (long long gi = (long long)blockIdx.x * kThreads + threadIdx.x; gi < n;
+       gi += (long long)gridDim.x * kThreads) {
+    const int h = (int)(gi / per_head);
+    const long long r = gi - (long long)h * per_head;
+    const int t = (int)(r / g.gpd), grp = (int)(r - (long long)t * g.gpd);
+    const int page = t / kPagePositions;
+    const uint8_t *pp = buf + (((size_t)lkv * g.n_heads + h) * g.n_pages + page) * g.page_bytes;
+    const float2 sb = reinterpret_cast<const float2 *>(pp + g.nib_bytes)
+                          [(t - page * kPagePositions) * g.gpd + grp];
+    const int code = is_nan_bits(sb.x) ? 1 : is_nan_bits(sb.y) ? 2 : (sb.x < 0.0f ? 3 : 0);
+    if (code) {
+      best = min(best, (unsigned long long)gi * 4 + code);
+      break;   // later groups of this thread have larger indices
+    }
+  }
+  // reduce over the warp, one atomic per warp that found something
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other < best ? other : best;
+  }
+  if ((threadIdx.x & 31) == 0 && best != ~0ull) atomicMin(keys + lkv, best);
+}
+
+__global__ void __launch_bounds__(kThreads)
+dequant_kernel(const uint8_t *__restrict__ buf, PageGeom g, int head_dim, int lkv, int pos_begin,
+               int n_pos, float *__restrict__ out) {
+  const long long total = (long long)g.n_heads * n_pos * head_dim;
+  for (long long i = (long long)blockIdx.x * kThreads + threadIdx.x; i < total;
+       i += (long long)gridDim.x * kThreads) {
+    const long long row = i / head_dim;
+    const int d = (int)(i - row * head_dim);
+    const int h = (int)(row / n_pos);
+    const int t = pos_begin + (int)(row - (long long)h * n_pos);
+    const int page = t / kPagePositions, pip = t - page * kPagePositions;
+    const uint8_t *pp = buf + (((size_t)lkv * g.n_heads + h) * g.n_pages + page) * g.page_bytes;
+    const int grp = d >> 6, k = d & 63;
+    const int slot = pip * g.gpd + grp;
+    const uint8_t byte = pp[(size_t)slot * 32 + (k & 31)];
+    const float2 sb = reinterpret_cast<const float2 *>(pp + g.nib_bytes)[slot];
+    out[i] = fmaf((float)(k < 32 ? (byte & 15) : (byte >> 4)), sb.x, sb.y);
+  }
+}
+
+int grid_cap(long long units) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  long long b = (units + kThreads - 1) / kThreads;
+  const long long cap = (long long)sms * 8;
+  return (int)(b < 1 ? 1 : (b > cap ? cap : b));
+}
+
+int dequant_check(const eakv_cache_t *c, int layer, int kv, int pos_begin, int pos_end,
+                  const void *out, const char *what) {
+  if (!c || !out || layer < 0 || layer >= c->n_layers || kv < 0 || kv > 1 || pos_begin < 0 ||
+      pos_end < pos_begin || pos_end > c->seq_len || c->geom.gpd == 0) {
+    set_error(EAKV_ERR_INVALID, "%s: invalid argument", what);
+    return EAKV_ERR_INVALID;
+  }
+  return EAKV_OK;
+}
+
+}  // namespace
+}  // namespace eakv
+
+using namespace eakv;
+
+extern "C" {
+
+int eakv_cache_validate(const eakv_cache_t *cc, int32_t *codes) {
+  clear_error();
+  if (!cc || !codes) {
+    set_error(EAKV_ERR_INVALID, "validate: invalid argument");
+    return EAKV_ERR_INVALID;
+  }
+  eakv_cache_t *c = const_cast<eakv_cache_t *>(cc);
+  const int n = c->n_layers * 2;
+  for (int i = 0; i < n; i++) codes[i] = 0;
+  if (c->seq_len == 0 || c->geom.gpd == 0) return EAKV_OK;
+  DeviceGuard g(c->device);
+  unsigned long long *d_keys = (unsigned long long *)cache_scratch(c, (size_t)n * 8);
+  if (!d_keys) return EAKV_ERR_ALLOC;
+  int rc = check_cuda(cudaMemsetAsync(d_keys, 0xFF, (size_t)n * 8, c->stream), "validate");
+  if (rc) return rc;
+  const long long groups = (long long)c->n_kv_heads * c->seq_len * c->geom.gpd;
+  int bx = grid_cap(groups) / n;
+  if (bx < 1) bx = 1;
+  validate_kernel<<<dim3(bx, n), kThreads, 0, c->stream>>>(c->d_buf, c->geom, c->seq_len, d_keys);
+  rc = check_cuda(cudaGetLastError(), "validate: launch");
+  if (rc) return rc;
+  unsigned long long *keys = new unsigned long long[n];
+  rc = check_cuda(cudaMemcpyAsync(keys, d_keys, (size_t)n * 8, cudaMemcpyDeviceToHost, c->stream),
+                  "validate: copy");
+  if (!rc) rc = check_cuda(cudaStreamSynchronize(c->stream), "validate");
+  if (!rc)
+    for (int i = 0; i < n; i++) codes[i] = keys[i] == ~0ull ? 0 : (int32_t)(keys[i] & 3);
+  delete[] keys;
+  return rc;
+}
+
+int eakv_cache_dequantize_device(const eakv_cache_t *c, int layer, int kv_idx, int pos_begin,
+                                 int pos_end, float *d_out, void *stream) {
+  clear_error();
+  int rc = dequant_check(c, layer, kv_idx, pos_begin, pos_end, d_out, "dequantize_device");
+  if (rc) return rc;
+  const int n_pos = pos_end - pos_begin;
+  if (n_pos == 0) return EAKV_OK;
+  DeviceGuard g(c->device);
+  const long long total = (long long)c->n_kv_heads * n_pos * c->head_dim;
+  cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+  dequant_kernel<<<grid_cap(total), kThreads, 0, s>>>(c->d_buf, c->geom, c->head_dim,
+                                                      layer * 2 + kv_idx, pos_begin, n_pos, d_out);
+  return check_cuda(cudaGetLastError(), "dequantize_device: launch");
+}
+
+int eakv_cache_dequantize(const eakv_cache_t *cc, int layer, int kv_idx, int pos_begin,
+                          int pos_end, float *out) {
+  clear_error();
+  int rc = dequant_check(cc, layer, kv_idx, pos_begin, pos_end, out, "dequantize");
+  if (rc) return rc;
+  eakv_cache_t *c = const_cast<eakv_cache_t *>(cc);
+  const size_t bytes = (size_t)c->n_kv_heads * (pos_end - pos_begin) * c->head_dim * sizeof(float);
+  if (bytes == 0) return EAKV_OK;
+  DeviceGuard g(c->device);
+  float *d_out = (float *)cache_scratch(c, bytes);
+  if (!d_out) return EAKV_ERR_ALLOC;
+  rc = eakv_cache_dequantize_device(c, layer, kv_idx, pos_begin, pos_end, d_out, c->stream);
+  if (rc) return rc;
+  rc = check_cuda(cudaMemcpyAsync(out, d_out, bytes, cudaMemcpyDeviceToHost, c->stream),
+                  "dequantize: copy");
+  if (rc) return rc;
+  return check_cuda(cudaStreamSynchronize(c->stream), "dequantize");
+}
+
+}  // extern "C"

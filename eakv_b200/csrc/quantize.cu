@@ -13,10 +13,12 @@
 //   * between -0.0 and +0.0 the first one in element order wins, so when
 //     the min (or max) is a zero the kernel looks up the first zero.
 //
-// Mapping: 8 threads per 64-float group. Thread j loads elements 4j..4j+3
-// (the low nibbles of bytes 4j..4j+3) and 32+4j..32+4j+3 (their high
-// nibbles) as two 16-byte loads, and stores the 4 packed bytes as one
-// 32-bit word, so a warp moves 4 groups with fully coalesced traffic.
+// Mapping: 4 threads per 64-float group. Thread j loads elements 8j..8j+7
+// (the low nibbles of bytes 8j..8j+7) and 32+8j..32+8j+7 (their high
+// nibbles) as four 16-byte loads, and stores the 8 packed bytes as one
+// 8-byte word, so a warp moves 8 groups with fully coalesced traffic and
+// the per-group work (min/max reduction, the two divisions) is shared by
+// 8 groups per warp instruction.
 // HBM-bound: 256 B read + 40 B written per group.
 //
 // The cache keeps, per (layer, KV head), the largest biased exponent of any
@@ -30,6 +32,7 @@ namespace eakv {
 namespace {
 
 constexpr int kThreads = 256;
+constexpr int kTPG = 4;   // threads per 64-element group
 
 // The reference truncates with x86 cvttss2si, which returns INT_MIN for NaN
 // and for anything outside the int32 range; the clamp then gives 0. That
@@ -47,16 +50,20 @@ template <bool kVec>
 __global__ void __launch_bounds__(kThreads)
 quantize_kernel(const float *__restrict__ src, uint8_t *__restrict__ dst, PageGeom g,
                 int unit_base, long long n_groups, int n_tok, int pos0, int head_dim) {
+  constexpr int EPT = 32 / kTPG;          // elements per thread in each half of the group
+  constexpr int GPW = 32 / kTPG;          // groups per warp and iteration
   const long long groups_per_unit = (long long)n_tok * g.gpd;
   const int lane = threadIdx.x & 31;
-  const int j = lane & 7;                 // thread within the group
+  const int j = lane % kTPG;              // thread within the group
   const long long warps = (long long)gridDim.x * (kThreads / 32);
   const long long warp_id = (long long)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
 
-  for (long long gb = warp_id * 4; gb < n_groups; gb += warps * 4) {
-    const long long gi = gb + (lane >> 3);
+  for (long long gb = warp_id * GPW; gb < n_groups; gb += warps * GPW) {
+    const long long gi = gb + lane / kTPG;
     const bool valid = gi < n_groups;
-    float v[8];
+    // v[e]: element EPT*j + e (low nibble of byte EPT*j + e); v[EPT + e]:
+    // element 32 + EPT*j + e (its high nibble)
+    float v[2 * EPT];
     long long u = 0, gih = 0;
     if (valid) {
       // Group gih of unit u: the reference quantizes n_tok*gpd consecutive
@@ -66,34 +73,40 @@ quantize_kernel(const float *__restrict__ src, uint8_t *__restrict__ dst, PageGe
       gih = gi - u * groups_per_unit;
       const float *x = src + (size_t)u * n_tok * head_dim + (size_t)gih * 64;
       if (kVec) {
-        float4 a = *reinterpret_cast<const float4 *>(x + 4 * j);
-        float4 b = *reinterpret_cast<const float4 *>(x + 32 + 4 * j);
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+#pragma unroll
+          for (int k = 0; k < EPT / 4; k++) {
+            const float4 a = *reinterpret_cast<const float4 *>(x + 32 * h + EPT * j + 4 * k);
+            v[h * EPT + 4 * k + 0] = a.x;
+            v[h * EPT + 4 * k + 1] = a.y;
+            v[h * EPT + 4 * k + 2] = a.z;
+            v[h * EPT + 4 * k + 3] = a.w;
+          }
       } else {
 #pragma unroll
-        for (int e = 0; e < 4; e++) {
-          v[e] = x[4 * j + e];
-          v[4 + e] = x[32 + 4 * j + e];
+        for (int e = 0; e < EPT; e++) {
+          v[e] = x[EPT * j + e];
+          v[EPT + e] = x[32 + EPT * j + e];
         }
       }
     } else {
 #pragma unroll
-      for (int e = 0; e < 8; e++) v[e] = 0.0f;
+      for (int e = 0; e < 2 * EPT; e++) v[e] = 0.0f;
     }
 
     float mn = v[0], mx = v[0];
 #pragma unroll
-    for (int e = 1; e < 8; e++) {
+    for (int e = 1; e < 2 * EPT; e++) {
       mn = fminf(mn, v[e]);
       mx = fmaxf(mx, v[e]);
     }
 #pragma unroll
-    for (int o = 1; o < 8; o <<= 1) {
+    for (int o = 1; o < kTPG; o <<= 1) {
       mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     }
-    const float x0 = __shfl_sync(0xffffffffu, v[0], lane & 24);
+    const float x0 = __shfl_sync(0xffffffffu, v[0], lane & ~(kTPG - 1));
 
     // Signed-zero fix-up (rare, warp-uniform branch): the reference keeps
     // the first zero it meets, whichever its sign.
@@ -102,15 +115,15 @@ quantize_kernel(const float *__restrict__ src, uint8_t *__restrict__ dst, PageGe
       int fz = 64;
       float zv = 0.0f;
 #pragma unroll
-      for (int e = 7; e >= 0; e--) {
-        int idx = e < 4 ? 4 * j + e : 32 + 4 * j + (e - 4);
+      for (int e = 2 * EPT - 1; e >= 0; e--) {
+        int idx = e < EPT ? EPT * j + e : 32 + EPT * j + (e - EPT);
         if (v[e] == 0.0f && idx < fz) {
           fz = idx;
           zv = v[e];
         }
       }
 #pragma unroll
-      for (int o = 1; o < 8; o <<= 1) {
+      for (int o = 1; o < kTPG; o <<= 1) {
         int ofz = __shfl_xor_sync(0xffffffffu, fz, o);
         float ozv = __shfl_xor_sync(0xffffffffu, zv, o);
         if (ofz < fz) {
@@ -134,12 +147,16 @@ quantize_kernel(const float *__restrict__ src, uint8_t *__restrict__ dst, PageGe
       scale = __fdiv_rn(range, 15.0f);
       inv = __fdiv_rn(15.0f, range);
     }
-    uint32_t word = 0;
+    uint32_t word[EPT / 4];
 #pragma unroll
-    for (int e = 0; e < 4; e++) {
-      uint32_t lo = (uint32_t)quant_one(v[e], mn, inv);
-      uint32_t hi = (uint32_t)quant_one(v[4 + e], mn, inv);
-      word |= (hi * 16u + lo) << (8 * e);
+    for (int w = 0; w < EPT / 4; w++) {
+      word[w] = 0;
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        uint32_t lo = (uint32_t)quant_one(v[4 * w + e], mn, inv);
+        uint32_t hi = (uint32_t)quant_one(v[EPT + 4 * w + e], mn, inv);
+        word[w] |= (hi * 16u + lo) << (8 * e);
+      }
     }
     if (valid) {
       const int t = (int)(gih / g.gpd);
@@ -149,10 +166,13 @@ quantize_kernel(const float *__restrict__ src, uint8_t *__restrict__ dst, PageGe
       const int pip = pos - page * kPagePositions;
       uint8_t *pp = dst + ((size_t)(unit_base + u) * g.n_pages + page) * g.page_bytes;
       const int slot = pip * g.gpd + grp;
-      *reinterpret_cast<uint32_t *>(pp + (size_t)slot * 32 + 4 * j) = word;
-      if (j == 0) {
+      uint8_t *wp = pp + (size_t)slot * 32 + EPT * j;
+      if (EPT == 8)
+        *reinterpret_cast<uint2 *>(wp) = make_uint2(word[0], word[EPT / 4 - 1]);
+      else
+        *reinterpret_cast<uint32_t *>(wp) = word[0];
+      if (j == 0)
         *reinterpret_cast<float2 *>(pp + g.nib_bytes + (size_t)slot * 8) = make_float2(scale, mn);
-      }
     }
   }
 }
@@ -195,7 +215,8 @@ cudaError_t launch_quantize(const PageGeom &g, uint8_t *d_buf, const float *d_sr
                             cudaStream_t s) {
   if (g.gpd <= 0 || n_units <= 0 || n_tok <= 0) return cudaSuccess;
   const long long n_groups = (long long)n_units * n_tok * g.gpd;
-  long long blocks = (n_groups + 31) / 32;
+  constexpr int kGroupsPerBlock = kThreads / kTPG;
+  long long blocks = (n_groups + kGroupsPerBlock - 1) / kGroupsPerBlock;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

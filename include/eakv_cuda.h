@@ -139,6 +139,27 @@ int eakv_lse_combine(int n_parts, int n_rows, int head_dim,
                      const float *d_parts, const float *d_lse,
                      float *d_output, float *d_lse_out, void *stream);
 
+/* ---- inspecting a resident cache ------------------------------------------ */
+
+/* Device validate: the reference's q4_validate (kernels/validate.ea:14-71) as
+ * its CLI runs it on every (layer, K/V) block (src/cli.c:39-98), without
+ * copying the cache to the host. codes (host, n_layers*2 entries, index
+ * layer*2 + kv) receive 0 (ok), 1 (NaN scale), 2 (NaN bias) or 3 (negative
+ * scale) for the first failing group in the reference's order ([head]
+ * [position][group], positions < seq_len). Returns EAKV_OK or an error. */
+int eakv_cache_validate(const eakv_cache_t *cache, int32_t *codes);
+
+/* Dequantize positions [pos_begin, pos_end) of one (layer, K/V) block into
+ * f32 [n_kv_heads][pos_end - pos_begin][head_dim], value = nibble * scale +
+ * bias with one rounding (reference kernels/dequantize_avx512.ea:10-89, whose
+ * range form :52-89 this generalises). The _device form writes device
+ * memory on `stream` (NULL: the cache's stream); the other writes host
+ * memory and returns when done. EAKV_ERR_INVALID for a bad block or range. */
+int eakv_cache_dequantize_device(const eakv_cache_t *cache, int layer, int kv_idx, int pos_begin,
+                                 int pos_end, float *d_out, void *stream);
+int eakv_cache_dequantize(const eakv_cache_t *cache, int layer, int kv_idx, int pos_begin,
+                          int pos_end, float *out);
+
 /* ---- testing aid ------------------------------------------------------ */
 
 /* Forces every later fused / decode call on this host thread to cut each

@@ -1,6 +1,6 @@
-"""CPU: the C-ABI library loads and exports every function that
-include/eakv.h and include/eakv_cuda.h declare, and the Python binding
-covers all of them. No kernel runs here."""
+"""CPU: the C-ABI library loads and exports every function that the headers
+in include/ declare, and the Python binding covers all of them. No kernel
+runs here."""
 import ctypes
 import os
 import re
@@ -9,7 +9,8 @@ import pytest
 
 from conftest import ROOT
 
-HEADERS = [os.path.join(ROOT, "include", h) for h in ("eakv.h", "eakv_cuda.h")]
+HEADERS = [os.path.join(ROOT, "include", h)
+           for h in ("eakv.h", "eakv_cuda.h", "eakv_ggml.h", "eakv_llama.h")]
 
 
 def declared_functions():
@@ -30,6 +31,10 @@ def test_headers_declare_reference_api():
            "eakv_attention_scores", "eakv_attention_output", "eakv_cache_save",
            "eakv_cache_load", "eakv_cache_seq_len", "eakv_cache_n_layers", "eakv_cache_n_heads",
            "eakv_cache_head_dim", "eakv_cache_max_seq_len", "eakv_cache_compression_ratio"]
+    # reference include/eakv_ggml.h:36-52
+    ref += ["eakv_quantize_row", "eakv_dequantize_row", "eakv_vec_dot_q4_f32"]
+    # reference include/eakv_llama.h:26-41
+    ref += ["eakv_from_llama_state", "eakv_from_llama_state_append"]
     for r in ref:
         assert r in names
 
