@@ -630,14 +630,123 @@ def run_ggml(args, world, rank, local):
         }), flush=True)
 
 
+def _line(name, value, unit, ms, args, workload, nbytes=None, cpu=None, launches=None):
+    peak, peak_kind = measured_peak()
+    roof = None
+    if nbytes is not None:
+        gbs = nbytes / (ms / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                "frac": gbs / peak, "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
+                "algorithmic_bytes_per_launch": nbytes}
+    print(json.dumps({
+        "metric": name, "value": value, "unit": unit, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": {"workload": workload, "l2": "inputs larger than L2, no flush"},
+        "roofline": roof, "cpu_baseline": cpu, "gpu_launches": launches,
+    }), flush=True)
+
+
+def _time(fn, args, stream):
+    import torch
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / args.steps
+
+
+def run_inspect(args, world, rank, local):
+    """Device validate and dequantize (SURVEY next rows 3, 4) on one cfg4
+    sequence (32 layers x 8 KV heads x 32768 positions, 1.34 GB of pages)."""
+    import torch
+    import eakv_b200 as E
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    E.set_device(local)
+    dev = torch.device("cuda", local)
+    cfg = dict(CONFIGS[4], B=1)
+    (c,) = build_caches(E, torch, cfg, dev, seed=7)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    c.set_stream(stream.cuda_stream)
+    L, H, hd, S = cfg["L"], cfg["nkv"], cfg["hd"], cfg["S"]
+    groups = L * 2 * H * S * hd // 64
+    ms = _time(lambda: c.validate(), args, stream)
+    _line("device validate GB/s (scale/bias bytes read)", groups * 8 / (ms / 1e3) / 1e9, "GB/s", ms,
+          args, f"validate: cfg4 sequence, {groups} groups, codes copied back each call",
+          nbytes=groups * 8, launches=args.steps)
+    out = torch.empty(H, S, hd, device=dev)
+    ms = _time(lambda: c.dequantize_device(5, 1, 0, S, out, stream.cuda_stream), args, stream)
+    nb = H * S * hd // 64 * 40 + H * S * hd * 4
+    _line("dequantize GB/s (Q4 read + f32 written)", nb / (ms / 1e3) / 1e9, "GB/s", ms, args,
+          f"dequantize one (layer, V) block: {H} heads x {S} positions x {hd}", nbytes=nb,
+          launches=args.steps)
+    c.free()
+
+
+def run_llama(args, world, rank, local):
+    """llama.cpp state import (SURVEY next row 2): host state buffer in,
+    device cache out, PCIe inside the timed region (the API's own
+    contract); the reference bridge on the host cores beside it."""
+    import ctypes
+    import torch
+    import eakv_b200 as E
+    from oracle import oracle as O
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    E.set_device(local)
+    L, H, hd, cells = 32, 8, 128, 4096
+    rng = np.random.default_rng(0)
+    k = rng.standard_normal((L, cells, H * hd), dtype=np.float32).astype(np.float16)
+    state = O.llama_state(k, k, 1)
+    buf = np.frombuffer(state, np.uint8)
+    for _ in range(max(1, args.warmup // 2)):
+        E.Cache.from_llama_state(state, L, H, hd, cells).free()
+    t0 = time.time()
+    reps = max(1, min(args.steps, 5))
+    for _ in range(reps):
+        E.Cache.from_llama_state(state, L, H, hd, cells).free()
+    ms = (time.time() - t0) / reps * 1e3
+    cpu = None
+    if os.path.exists(O.REF_LLAMA_SO):
+        R = ctypes.CDLL(O.REF_LLAMA_SO)
+        R.eakv_from_llama_state.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int,
+                                            ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                            ctypes.POINTER(ctypes.c_void_p)]
+        R.eakv_cache_free.argtypes = [ctypes.c_void_p]
+        t0, n = time.time(), 0
+        while time.time() - t0 < args.cpu_seconds / 2 or n == 0:
+            cc = ctypes.c_void_p()
+            assert R.eakv_from_llama_state(buf.ctypes.data, buf.size, L, H, hd, cells,
+                                           ctypes.byref(cc)) == 0
+            R.eakv_cache_free(cc)
+            n += 1
+        cpu_s = (time.time() - t0) / n
+        cpu = {"value": buf.size / cpu_s / 1e9, "unit": "GB/s of state", "cores": 1,
+               "kind": "reference", "sample": f"{n} whole imports"}
+    _line("llama.cpp state import GB/s of state (host buffer -> device cache, wall clock)",
+          buf.size / (ms / 1e3) / 1e9, "GB/s of state", ms, args,
+          f"llama state: {L} layers x {H} KV heads x {hd} x {cells} cells, f16, v_trans=1 "
+          f"({buf.size / 1e9:.2f} GB)", cpu=cpu, launches=None)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", type=int, default=4, choices=sorted(CONFIGS))
-    ap.add_argument("--op", default="decode", choices=["decode", "ggml"],
-                    help="ggml: time the q4_1_eakv ggml block type kernels instead")
+    ap.add_argument("--op", default="decode", choices=["decode", "ggml", "inspect", "llama"],
+                    help="time another part instead: the q4_1_eakv ggml type kernels, device "
+                         "validate + dequantize, or the llama.cpp state import")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
@@ -665,6 +774,10 @@ def main():
     try:
         if args.op == "ggml":
             run_ggml(args, world, rank, local)
+        elif args.op == "inspect":
+            run_inspect(args, world, rank, local)
+        elif args.op == "llama":
+            run_llama(args, world, rank, local)
         elif args.impl == "reference":
             run_reference(args, cfg, world, rank)
         else:

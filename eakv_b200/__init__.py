@@ -214,7 +214,7 @@ class Cache:
 
     def dequantize(self, layer, kv_idx, pos_begin, pos_end):
         """f32[n_kv_heads][pos_end - pos_begin][head_dim] on the host."""
-        out = np.zeros((self.n_heads, pos_end - pos_begin, self.head_dim), np.float32)
+        out = np.zeros((self.n_kv_heads, max(pos_end - pos_begin, 0), self.head_dim), np.float32)
         _check(lib().eakv_cache_dequantize(self.h, layer, kv_idx, pos_begin, pos_end, _ptr(out)),
                "eakv_cache_dequantize")
         return out

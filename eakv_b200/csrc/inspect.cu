@@ -9,7 +9,7 @@
 // in parallel; a failing group offers the key index*4 + code to an
 // atomicMin per (layer, K/V), so the smallest key is the reference's first
 // failure and its low two bits its code. Only the (scale, bias) pairs are
-// read: 8 of every 40 bytes of the pages.
+// read (8 of every 40 bytes of the pages), page by page, contiguously.
 //
 // dequantize: value = fma(nibble, scale, bias) for the lo (element k) and
 // hi (element k+32) nibble of byte k of a group, the reference's f32x16
@@ -26,29 +26,36 @@ __device__ __forceinline__ bool is_nan_bits(float v) {
   return b > 2139095040 || (b < 0 && b > -8388608);
 }
 
+// Block (x, y): pages x*kPagesPerBlock.. of every head of block y =
+// layer*2 + kv; thread i takes slot i of each page's (scale, bias) array.
+constexpr int kPagesPerBlock = 8;
+
 __global__ void __launch_bounds__(kThreads)
 validate_kernel(const uint8_t *__restrict__ buf, PageGeom g, int seq_len,
                 unsigned long long *__restrict__ keys) {
   const int lkv = blockIdx.y;   // layer * 2 + kv
-  const long long per_head = (long long)seq_len * g.gpd;
-  const long long n = per_head * g.n_heads;
+  const int used_pages = (seq_len + kPagePositions - 1) / kPagePositions;
+  const int slots = kPagePositions * g.gpd;
   unsigned long long best = ~0ull;
-  for (long long gi = (long long)blockIdx.x * kThreads + threadIdx.x; gi < n;
-       gi += (long long)gridDim.x * kThreads) {
-    const int h = (int)(gi / per_head);
-    const long long r = gi - (long long)h * per_head;
-    const int t = (int)(r / g.gpd), grp = (int)(r - (long long)t * g.gpd);
-    const int page = t / kPagePositions;
-    const uint8_t *pp = buf + (((size_t)lkv * g.n_heads + h) * g.n_pages + page) * g.page_bytes;
-    const float2 sb = reinterpret_cast<const float2 *>(pp + g.nib_bytes)
-                          [(t - page * kPagePositions) * g.gpd + grp];
-    const int code = is_nan_bits(sb.x) ? 1 : is_nan_bits(sb.y) ? 2 : (sb.x < 0.0f ? 3 : 0);
-    if (code) {
-      best = min(best, (unsigned long long)gi * 4 + code);
-      break;   // later groups of this thread have larger indices
+  for (int h = 0; h < g.n_heads; h++) {
+    for (int pg = blockIdx.x * kPagesPerBlock;
+         pg < used_pages && pg < (int)(blockIdx.x + 1) * kPagesPerBlock; pg++) {
+      const float2 *sbp = reinterpret_cast<const float2 *>(
+          buf + (((size_t)lkv * g.n_heads + h) * g.n_pages + pg) * g.page_bytes + g.nib_bytes);
+      for (int sl = threadIdx.x; sl < slots; sl += kThreads) {
+        const int t = pg * kPagePositions + sl / g.gpd;
+        if (t >= seq_len) break;
+        const float2 sb = sbp[sl];
+        const int code = is_nan_bits(sb.x) ? 1 : is_nan_bits(sb.y) ? 2 : (sb.x < 0.0f ? 3 : 0);
+        if (code) {
+          // dense index of the group: [head][position][group]
+          const unsigned long long gi =
+              ((unsigned long long)h * seq_len + t) * g.gpd + (sl - (sl / g.gpd) * g.gpd);
+          best = min(best, gi * 4 + code);
+        }
+      }
     }
   }
-  // reduce over the warp, one atomic per warp that found something
   for (int o = 16; o > 0; o >>= 1) {
     const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
     best = other < best ? other : best;
@@ -56,23 +63,35 @@ validate_kernel(const uint8_t *__restrict__ buf, PageGeom g, int seq_len,
   if ((threadIdx.x & 31) == 0 && best != ~0ull) atomicMin(keys + lkv, best);
 }
 
+// One warp per (head, position) row; lane l writes dims 4l..4l+3 of each
+// 128-dim slice: four consecutive dims are four consecutive bytes of one
+// group, all low or all high nibbles.
 __global__ void __launch_bounds__(kThreads)
 dequant_kernel(const uint8_t *__restrict__ buf, PageGeom g, int head_dim, int lkv, int pos_begin,
                int n_pos, float *__restrict__ out) {
-  const long long total = (long long)g.n_heads * n_pos * head_dim;
-  for (long long i = (long long)blockIdx.x * kThreads + threadIdx.x; i < total;
-       i += (long long)gridDim.x * kThreads) {
-    const long long row = i / head_dim;
-    const int d = (int)(i - row * head_dim);
+  const int lane = threadIdx.x & 31;
+  const long long rows = (long long)g.n_heads * n_pos;
+  const long long warps = (long long)gridDim.x * (kThreads / 32);
+  for (long long row = (long long)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < rows;
+       row += warps) {
     const int h = (int)(row / n_pos);
     const int t = pos_begin + (int)(row - (long long)h * n_pos);
     const int page = t / kPagePositions, pip = t - page * kPagePositions;
     const uint8_t *pp = buf + (((size_t)lkv * g.n_heads + h) * g.n_pages + page) * g.page_bytes;
-    const int grp = d >> 6, k = d & 63;
-    const int slot = pip * g.gpd + grp;
-    const uint8_t byte = pp[(size_t)slot * 32 + (k & 31)];
-    const float2 sb = reinterpret_cast<const float2 *>(pp + g.nib_bytes)[slot];
-    out[i] = fmaf((float)(k < 32 ? (byte & 15) : (byte >> 4)), sb.x, sb.y);
+    float *o = out + row * head_dim;
+    for (int d = 4 * lane; d < head_dim; d += 128) {
+      const int grp = d >> 6, k = d & 63;
+      const int slot = pip * g.gpd + grp;
+      const uint32_t w = *reinterpret_cast<const uint32_t *>(pp + (size_t)slot * 32 + (k & 31));
+      const float2 sb = reinterpret_cast<const float2 *>(pp + g.nib_bytes)[slot];
+      const int sh = k < 32 ? 0 : 4;
+      float4 v;
+      v.x = fmaf((float)((w >> sh) & 15), sb.x, sb.y);
+      v.y = fmaf((float)((w >> (8 + sh)) & 15), sb.x, sb.y);
+      v.z = fmaf((float)((w >> (16 + sh)) & 15), sb.x, sb.y);
+      v.w = fmaf((float)((w >> (24 + sh)) & 15), sb.x, sb.y);
+      *reinterpret_cast<float4 *>(o + d) = v;
+    }
   }
 }
 
@@ -117,9 +136,8 @@ int eakv_cache_validate(const eakv_cache_t *cc, int32_t *codes) {
   if (!d_keys) return EAKV_ERR_ALLOC;
   int rc = check_cuda(cudaMemsetAsync(d_keys, 0xFF, (size_t)n * 8, c->stream), "validate");
   if (rc) return rc;
-  const long long groups = (long long)c->n_kv_heads * c->seq_len * c->geom.gpd;
-  int bx = grid_cap(groups) / n;
-  if (bx < 1) bx = 1;
+  const int used_pages = (c->seq_len + kPagePositions - 1) / kPagePositions;
+  const int bx = (used_pages + kPagesPerBlock - 1) / kPagesPerBlock;
   validate_kernel<<<dim3(bx, n), kThreads, 0, c->stream>>>(c->d_buf, c->geom, c->seq_len, d_keys);
   rc = check_cuda(cudaGetLastError(), "validate: launch");
   if (rc) return rc;
@@ -138,13 +156,18 @@ int eakv_cache_dequantize_device(const eakv_cache_t *c, int layer, int kv_idx, i
   clear_error();
   int rc = dequant_check(c, layer, kv_idx, pos_begin, pos_end, d_out, "dequantize_device");
   if (rc) return rc;
+  if ((uintptr_t)d_out & 15) {   // rows are written as 16-byte vectors
+    set_error(EAKV_ERR_INVALID, "dequantize_device: d_out must be 16-byte aligned");
+    return EAKV_ERR_INVALID;
+  }
   const int n_pos = pos_end - pos_begin;
   if (n_pos == 0) return EAKV_OK;
   DeviceGuard g(c->device);
-  const long long total = (long long)c->n_kv_heads * n_pos * c->head_dim;
+  const long long rows = (long long)c->n_kv_heads * n_pos;
   cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
-  dequant_kernel<<<grid_cap(total), kThreads, 0, s>>>(c->d_buf, c->geom, c->head_dim,
-                                                      layer * 2 + kv_idx, pos_begin, n_pos, d_out);
+  dequant_kernel<<<grid_cap(rows * 32), kThreads, 0, s>>>(c->d_buf, c->geom, c->head_dim,
+                                                          layer * 2 + kv_idx, pos_begin, n_pos,
+                                                          d_out);
   return check_cuda(cudaGetLastError(), "dequantize_device: launch");
 }
 

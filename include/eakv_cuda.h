@@ -153,8 +153,9 @@ int eakv_cache_validate(const eakv_cache_t *cache, int32_t *codes);
  * f32 [n_kv_heads][pos_end - pos_begin][head_dim], value = nibble * scale +
  * bias with one rounding (reference kernels/dequantize_avx512.ea:10-89, whose
  * range form :52-89 this generalises). The _device form writes device
- * memory on `stream` (NULL: the cache's stream); the other writes host
- * memory and returns when done. EAKV_ERR_INVALID for a bad block or range. */
+ * memory on `stream` (NULL: the cache's stream; d_out 16-byte aligned); the
+ * other writes host memory and returns when done. EAKV_ERR_INVALID for a bad
+ * block, range or alignment. */
 int eakv_cache_dequantize_device(const eakv_cache_t *cache, int layer, int kv_idx, int pos_begin,
                                  int pos_end, float *d_out, void *stream);
 int eakv_cache_dequantize(const eakv_cache_t *cache, int layer, int kv_idx, int pos_begin,
