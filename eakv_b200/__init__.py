@@ -24,7 +24,8 @@ EAKV_ERR_ALLOC = -3
 EAKV_ERR_INVALID = -4
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libeakv_b200.so")
+# EAKV_B200_LIB selects another build of the library (same ABI)
+LIB_PATH = os.environ.get("EAKV_B200_LIB") or os.path.join(_HERE, "libeakv_b200.so")
 
 _c = ctypes
 _P = _c.c_void_p
