@@ -491,6 +491,9 @@ static Plan plan(DecodeArgs &a, const DecodeBatch &batch) {
   if (max_pages > 1) {
     long long target = 8LL * resident;
     ns = (int)((target + p.items - 1) / p.items);
+    // the tensor-core kernel works on two pages at a time (two warps per
+    // page): a split of one page would leave half its warps idle
+    if (p.mma_gh && ns > max_pages / 2) ns = max_pages / 2 > 0 ? max_pages / 2 : 1;
     if (a.force_splits > 0) ns = a.force_splits;
     if (ns > max_pages) ns = max_pages;
     if (ns < 1) ns = 1;
