@@ -472,6 +472,8 @@ struct Plan {
   int items;
 };
 
+constexpr int kMaxSplitPages = 256;   // 16384 positions
+
 static Plan plan(DecodeArgs &a, const DecodeBatch &batch) {
   const int G = a.n_q_heads / a.geom.n_heads;
   Plan p;
@@ -494,6 +496,12 @@ static Plan plan(DecodeArgs &a, const DecodeBatch &batch) {
     // the tensor-core kernel works on two pages at a time (two warps per
     // page): a split of one page would leave half its warps idle
     if (p.mma_gh && ns > max_pages / 2) ns = max_pages / 2 > 0 ? max_pages / 2 : 1;
+    // ... and its f32 tensor-core accumulators drift with the number of
+    // accumulation steps (1.1e-4 absolute after 512 pages of one row, on
+    // outputs of ~0.02; about half that at 256): no split is longer than
+    // kMaxSplitPages pages
+    if (p.mma_gh && ns < (max_pages + kMaxSplitPages - 1) / kMaxSplitPages)
+      ns = (max_pages + kMaxSplitPages - 1) / kMaxSplitPages;
     if (a.force_splits > 0) ns = a.force_splits;
     if (ns > max_pages) ns = max_pages;
     if (ns < 1) ns = 1;
