@@ -37,11 +37,6 @@ constexpr int kBlockBytes = 40;
 __device__ __forceinline__ float minps(float a, float b) { return a < b ? a : b; }
 __device__ __forceinline__ float maxps(float a, float b) { return a > b ? a : b; }
 
-// x86 cvttps2dq: truncation, INT32_MIN for NaN and out-of-range values
-__device__ __forceinline__ int cvtt(float v) {
-  return (v >= -2147483648.0f && v < 2147483648.0f) ? __float2int_rz(v) : (int)0x80000000;
-}
-
 // Lanes of this thread's half warp: the loops below run per half warp, and
 // the two halves of a warp may leave them at different trips, so every
 // shuffle names only its own half.
@@ -90,10 +85,13 @@ ggml_quantize_kernel(const float *__restrict__ src, uint8_t *__restrict__ dst, l
     const float range = __fsub_rn(mx, mn);
     const float d = __fdiv_rn(range, 15.0f);
     const float id = range > 0.0f ? __fdiv_rn(15.0f, range) : 0.0f;
+    // after the clamp t is in [0, 15] or NaN; cvtt(t) is then floor(t), the
+    // low 4 bits of t + 2^23 added toward zero, or for NaN INT32_MIN, whose
+    // low byte and whose value shifted left by 4 are both 0
     auto q = [&](float v) {
       float t = __fmul_rn(__fsub_rn(v, mn), id);
       t = minps(15.0f, maxps(0.0f, __fadd_rn(t, 0.5f)));
-      return (unsigned)cvtt(t);
+      return t == t ? ((unsigned)__float_as_int(__fadd_rz(t, 8388608.0f)) & 15u) : 0u;
     };
     uint8_t *blk = dst + i * kBlockBytes;
     blk[l] = (uint8_t)((q(x0) | (q(x2) << 4)) & 0xFF);
