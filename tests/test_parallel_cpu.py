@@ -184,3 +184,42 @@ def test_head_shards_times_sequence_split_gloo(world, seq_shards, S):
         assert p.exitcode == 0
     for rank, ok, err in results:
         assert ok, f"rank {rank}: max err {err}"
+
+
+def _worker_lost(rank, world, port, result_q):
+    """Rank 1 leaves between steps (after one merged step); rank 0's next
+    gather must end with an error, not hang."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=10))
+    part = torch.full((4, 8), float(rank))
+    parts = [torch.empty_like(part) for _ in range(world)]
+    dist.all_gather(parts, part)                   # one good step
+    if rank == 1:
+        result_q.put((rank, "left"))
+        result_q.close()
+        result_q.join_thread()                     # the message is out before the exit
+        os._exit(0)                                # no further collective, no clean shutdown
+    try:
+        dist.all_gather(parts, part)
+        result_q.put((rank, "no error"))
+    except Exception as e:                         # noqa: BLE001 - any error ends the wait
+        result_q.put((rank, f"raised {type(e).__name__}"))
+
+
+def test_lost_rank_ends_the_next_gather_with_an_error():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_lost, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert results[1] == "left"
+    assert results[0].startswith("raised"), results[0]
