@@ -27,32 +27,49 @@ __device__ __forceinline__ bool is_nan_bits(float v) {
 }
 
 // Block (x, y): pages x*kPagesPerBlock.. of every head of block y =
-// layer*2 + kv; thread i takes slot i of each page's (scale, bias) array.
+// layer*2 + kv; its threads take the (head, page, slot) units in order,
+// kUnroll loads at a time.
 constexpr int kPagesPerBlock = 8;
 
 __global__ void __launch_bounds__(kThreads)
 validate_kernel(const uint8_t *__restrict__ buf, PageGeom g, int seq_len,
                 unsigned long long *__restrict__ keys) {
-  const int lkv = blockIdx.y;   // layer * 2 + kv
+  constexpr int kUnroll = 4;   // loads in flight per thread
+  const int lkv = blockIdx.y;  // layer * 2 + kv
   const int used_pages = (seq_len + kPagePositions - 1) / kPagePositions;
+  const int pg0 = blockIdx.x * kPagesPerBlock;
+  const int n_pg = min(kPagesPerBlock, used_pages - pg0);
   const int slots = kPagePositions * g.gpd;
+  const int per_head = n_pg * slots;
+  const int total = g.n_heads * per_head;   // (head, page, slot) units of this block
   unsigned long long best = ~0ull;
-  for (int h = 0; h < g.n_heads; h++) {
-    for (int pg = blockIdx.x * kPagesPerBlock;
-         pg < used_pages && pg < (int)(blockIdx.x + 1) * kPagesPerBlock; pg++) {
-      const float2 *sbp = reinterpret_cast<const float2 *>(
-          buf + (((size_t)lkv * g.n_heads + h) * g.n_pages + pg) * g.page_bytes + g.nib_bytes);
-      for (int sl = threadIdx.x; sl < slots; sl += kThreads) {
-        const int t = pg * kPagePositions + sl / g.gpd;
-        if (t >= seq_len) break;
-        const float2 sb = sbp[sl];
-        const int code = is_nan_bits(sb.x) ? 1 : is_nan_bits(sb.y) ? 2 : (sb.x < 0.0f ? 3 : 0);
-        if (code) {
-          // dense index of the group: [head][position][group]
-          const unsigned long long gi =
-              ((unsigned long long)h * seq_len + t) * g.gpd + (sl - (sl / g.gpd) * g.gpd);
-          best = min(best, gi * 4 + code);
-        }
+  for (int u0 = threadIdx.x; u0 < total; u0 += kThreads * kUnroll) {
+    float2 sb[kUnroll];
+    int t[kUnroll], hh[kUnroll], sl[kUnroll];
+#pragma unroll
+    for (int k = 0; k < kUnroll; k++) {
+      const int u = u0 + k * kThreads;
+      t[k] = seq_len;   // marks "no unit"
+      if (u < total) {
+        const int h = u / per_head, r = u - h * per_head;
+        const int pg = pg0 + r / slots, s_ = r - (r / slots) * slots;
+        const float2 *sbp = reinterpret_cast<const float2 *>(
+            buf + (((size_t)lkv * g.n_heads + h) * g.n_pages + pg) * g.page_bytes + g.nib_bytes);
+        hh[k] = h;
+        sl[k] = s_;
+        t[k] = pg * kPagePositions + s_ / g.gpd;
+        if (t[k] < seq_len) sb[k] = sbp[s_];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kUnroll; k++) {
+      if (t[k] >= seq_len) continue;
+      const int code = is_nan_bits(sb[k].x) ? 1 : is_nan_bits(sb[k].y) ? 2 : (sb[k].x < 0.0f ? 3 : 0);
+      if (code) {
+        // dense index of the group: [head][position][group]
+        const unsigned long long gi = ((unsigned long long)hh[k] * seq_len + t[k]) * g.gpd +
+                                      (sl[k] - (sl[k] / g.gpd) * g.gpd);
+        best = min(best, gi * 4 + code);
       }
     }
   }
