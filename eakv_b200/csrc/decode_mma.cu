@@ -66,13 +66,17 @@ struct MCfg {
   static constexpr int VNT = RH == 8 ? 2 : 1;               // P' n-tiles (one per limb)
   static constexpr int VMT = 4 * NG;                        // output m-tiles of 16 dims
   static constexpr int NW = 4;                              // warps
-  static constexpr int WPP = 2;                             // warps per page
+  // warps per page: each warp takes whole pages (4 steps of 16 positions),
+  // the 4 warps of a CTA pages i, i+1, i+2, i+3 in turn
+  static constexpr int WPP = 1;
   static constexpr int THREADS = NW * 32;
   // CTAs per SM the register budget is cut for (128 registers at 4)
   static constexpr int MINB = (HD == 128 && RH == 8) ? 3 : 4;
   static constexpr int NIB = kPagePositions * NG * 32;
   static constexpr int PB = kPagePositions * NG * 40;
-  static constexpr int NSTAGE = HD == 128 ? 4 : 8;
+  // pages in flight: one per warp plus spares, as many as the shared memory
+  // of the CTAs that fit an SM allows (4 CTAs at 4 heads, 3 at 8)
+  static constexpr int NSTAGE = HD == 128 ? (RH == 8 ? 6 : 5) : 8;
   static constexpr int STAGE_BYTES = 2 * PB;
   static constexpr int RING = NSTAGE * STAGE_BYTES;
   static constexpr int MERGE_BYTES = NW * RH * (HD + 2) * 4;
@@ -442,7 +446,9 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
 
   // WPP warps share a page, each taking 64 / WPP positions as 16-position
   // steps; the NW / WPP warp groups take pages in turn, so the per-page
-  // costs (wait, release, loop) are paid once per 64 / WPP positions
+  // costs (wait, release, loop) are paid once per 64 / WPP positions. Page
+  // i lives in stage i % NSTAGE; its consumers release it and the last of
+  // them requests page i + NSTAGE into it.
   bool ok = true;
   const int wgrp = warp / C::WPP, wsub = warp % C::WPP;
   for (int i = wgrp; i < it.npages; i += C::NW / C::WPP) {
