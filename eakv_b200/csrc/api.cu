@@ -4,6 +4,8 @@
 #include <math.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "internal.cuh"
 
 namespace eakv {
@@ -110,6 +112,162 @@ int run_decode(const eakv_cache_t *c0, DecodeArgs &a, const DecodeBatch &b, size
     w = base + reserve;
   }
   return decode_launch(a, b, w, ws, s);
+}
+
+// ---- pipelined host-buffer decode -------------------------------------------
+
+// Below this many bytes of queries the host-buffer decode is one copy in, one
+// decode and one copy out on the caller's stream.
+constexpr size_t kPipelineMinBytes = 1u << 20;
+
+// Helper streams of the host-buffer decode on one device: queries in,
+// outputs out, and a second compute stream, so that the next chunk's CTAs
+// fill the SMs while the previous chunk's last CTAs drain. Created on first
+// use, kept for the life of the process.
+struct HostStreams {
+  cudaStream_t in = nullptr, out = nullptr, alt = nullptr;
+};
+std::mutex g_host_streams_mu;
+HostStreams g_host_streams[64];
+
+int host_streams(int dev, HostStreams &hs) {
+  std::lock_guard<std::mutex> lock(g_host_streams_mu);
+  if (dev < 0 || dev >= 64) {
+    set_error(EAKV_ERR_INVALID, "decode_attention_host: device %d out of range", dev);
+    return EAKV_ERR_INVALID;
+  }
+  HostStreams &h = g_host_streams[dev];
+  if (!h.in) {
+    cudaStream_t t[3] = {nullptr, nullptr, nullptr};
+    for (int i = 0; i < 3; i++) {
+      int rc = check_cuda(cudaStreamCreateWithFlags(&t[i], cudaStreamNonBlocking),
+                          "decode_attention_host: stream");
+      if (rc) {
+        for (int j = 0; j < i; j++) cudaStreamDestroy(t[j]);
+        return rc;
+      }
+    }
+    h.in = t[0];
+    h.out = t[1];
+    h.alt = t[2];
+  }
+  hs = h;
+  return EAKV_OK;
+}
+
+// Chunk boundaries over n units: a one-unit chunk first and last, whose
+// copies are the only ones not hidden behind a decode, and the rest in two
+// halves (n <= 4: one unit per chunk). Returns the number of chunks.
+int host_chunks(int n, int (&start)[5]) {
+  if (n < 2) {
+    start[0] = 0;
+    start[1] = n;
+    return 1;
+  }
+  if (n <= 4) {
+    for (int i = 0; i <= n; i++) start[i] = i;
+    return n;
+  }
+  const int mid = (n - 1) / 2;   // first half of the n - 2 middle units
+  start[0] = 0;
+  start[1] = 1;
+  start[2] = 1 + mid;
+  start[3] = n - 1;
+  start[4] = n;
+  return 4;
+}
+
+// The host-buffer decode in chunks of caches (or of layers, for a single
+// cache): the queries of every chunk are copied in on one stream, each
+// chunk's decode waits only for its own queries and alternates between the
+// caller's stream and a second one, and each chunk's outputs are copied
+// out as soon as its decode ends. Every chunk keeps the split plan of the
+// whole batch, so the outputs equal eakv_decode_attention's bit for bit.
+int decode_host_pipelined(const eakv_cache_t *const *caches, DecodeArgs a, const DecodeBatch &b,
+                          const float *queries, float *output, cudaStream_t s, int units,
+                          const int (&start)[5], int nch) {
+  const eakv_cache_t *c0 = caches[0];
+  const bool by_cache = a.n_caches > 1;
+  const size_t n = (size_t)a.n_caches * a.n_layers * a.n_q_heads * a.head_dim;
+  const size_t unit_floats = n / units;
+  const size_t half = (n * sizeof(float) + 255) / 256 * 256;
+  HostStreams hs;
+  int rc = host_streams(c0->device, hs);
+  if (rc) return rc;
+  decode_fix_plan(a, b);
+
+  DecodeArgs ca[4];
+  DecodeBatch cb[4];
+  size_t ws = 0;
+  for (int k = 0; k < nch; k++) {
+    const int u0 = start[k], cnt = start[k + 1] - start[k];
+    ca[k] = a;
+    if (by_cache) {
+      ca[k].n_caches = cnt;
+      fill_batch(cb[k], caches + u0, cnt);
+    } else {
+      ca[k].layer0 = u0;
+      ca[k].n_layers = cnt;
+      cb[k] = b;
+    }
+    const size_t w = decode_workspace_bytes(ca[k], cb[k]);
+    if (w > ws) ws = w;
+  }
+  ws = (ws + 255) / 256 * 256;
+  // [queries | outputs | workspace of stream s | workspace of the second stream]
+  uint8_t *base = (uint8_t *)cache_scratch(c0, 2 * half + 2 * ws);
+  if (!base) return EAKV_ERR_ALLOC;
+  float *dq = (float *)base, *dout = (float *)(base + half);
+
+  cudaEvent_t ev[9] = {};
+  int made = 0;
+  for (; made < 2 * nch + 1; made++) {
+    rc = check_cuda(cudaEventCreateWithFlags(&ev[made], cudaEventDisableTiming),
+                    "decode_attention_host: event");
+    if (rc) break;
+  }
+  cudaEvent_t ev0 = ev[0], *ev_in = ev + 1, *ev_done = ev + 1 + nch;
+  auto step = [&](cudaError_t e) {
+    if (!rc) rc = check_cuda(e, "decode_attention_host: pipeline");
+  };
+  if (!rc) {
+    // the copies in wait for earlier work on the caller's stream
+    step(cudaEventRecord(ev0, s));
+    step(cudaStreamWaitEvent(hs.in, ev0, 0));
+    step(cudaStreamWaitEvent(hs.alt, ev0, 0));
+    for (int k = 0; k < nch && !rc; k++) {
+      const size_t off = start[k] * unit_floats, cnt = (start[k + 1] - start[k]) * unit_floats;
+      step(cudaMemcpyAsync(dq + off, queries + off, cnt * sizeof(float), cudaMemcpyHostToDevice,
+                           hs.in));
+      step(cudaEventRecord(ev_in[k], hs.in));
+    }
+    // every decode is queued before any copy out, which blocks the host
+    // when the output buffer is pageable
+    for (int k = 0; k < nch && !rc; k++) {
+      cudaStream_t cs = (k & 1) ? hs.alt : s;
+      const size_t off = start[k] * unit_floats;
+      step(cudaStreamWaitEvent(cs, ev_in[k], 0));
+      if (rc) break;
+      ca[k].q = dq + off;
+      ca[k].out = dout + off;
+      rc = decode_launch(ca[k], cb[k], ws ? base + 2 * half + (k & 1) * ws : nullptr, ws, cs);
+      step(cudaEventRecord(ev_done[k], cs));
+    }
+    for (int k = 0; k < nch && !rc; k++) {
+      const size_t off = start[k] * unit_floats, cnt = (start[k + 1] - start[k]) * unit_floats;
+      step(cudaStreamWaitEvent(hs.out, ev_done[k], 0));
+      step(cudaMemcpyAsync(output + off, dout + off, cnt * sizeof(float), cudaMemcpyDeviceToHost,
+                           hs.out));
+    }
+  }
+  // nothing of this call is left in flight when it returns, error or not
+  const cudaStream_t all[4] = {hs.in, s, hs.alt, hs.out};
+  for (cudaStream_t t : all) {
+    cudaError_t e = cudaStreamSynchronize(t);
+    if (!rc && e != cudaSuccess) rc = check_cuda(e, "decode_attention_host");
+  }
+  for (int i = 0; i < made; i++) cudaEventDestroy(ev[i]);
+  return rc;
 }
 
 }  // namespace
@@ -242,6 +400,12 @@ int eakv_decode_attention_host(const eakv_cache_t *const *caches, int n_caches,
   DecodeArgs a = base_args(c0, n_caches, n_q);
   DecodeBatch b;
   fill_batch(b, caches, n_caches);
+  // units the batch can be cut into: caches, or the layers of a single cache
+  const int units = n_caches > 1 ? n_caches : c0->n_layers;
+  int start[5];
+  const int nch = n * sizeof(float) >= kPipelineMinBytes ? host_chunks(units, start) : 1;
+  if (nch > 1) return decode_host_pipelined(caches, a, b, queries, output, s, units, start, nch);
+
   size_t ws = decode_workspace_bytes(a, b);
   uint8_t *base = (uint8_t *)cache_scratch(c0, 2 * half + ws);
   if (!base) return EAKV_ERR_ALLOC;

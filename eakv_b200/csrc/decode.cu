@@ -103,7 +103,9 @@ decode_simt_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = a.n_q_heads / a.geom.n_heads;
   const int nhg = G / GC;
+  if (!launch_ok(a) || G % GC != 0) return;
   const Item it = decode_item(a, batch, nhg);
+  if (!item_ok(a, it, it.h * G + it.hg * GC, GC)) return;
   const size_t kv_stride = (size_t)a.geom.n_heads * a.geom.n_pages;   // pages from K to V
   const uint8_t *kpages =
       batch.base[it.b] + page_index(a.geom, it.layer, 0, it.h, 0) * C::PB;
@@ -130,7 +132,7 @@ decode_simt_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
     const uint32_t dst = smem_u32(smem + st * C::STAGE_BYTES);
     bulk_g2s(dst, kpages + (size_t)(it.pg0 + i) * C::PB, C::PB, full);
     bulk_g2s(dst + C::PB, vpages + (size_t)(it.pg0 + i) * C::PB, C::PB, full);
-    last_req[st] = i;
+    publish_requested(&last_req[st], i);
   };
   if (threadIdx.x == 0)
     for (int i = 0; i < it.npages && i < C::NSTAGE; i++) issue(i);
@@ -179,7 +181,8 @@ decode_simt_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
   bool ok = true;
   for (int i = 0; i < it.npages; i++) {
     const int st = i % C::NSTAGE;
-    if (!ok || !mbar_wait(smem_u32(&bars[st]), (i / C::NSTAGE) & 1, a.wait_budget)) {
+    if (!ok || !wait_requested(&last_req[st], i, a.wait_budget) ||
+        !mbar_wait(smem_u32(&bars[st]), (i / C::NSTAGE) & 1, a.wait_budget)) {
       atomicOr(a.status, kStatusWaitTimeout);
       ok = false;
       break;
@@ -282,6 +285,12 @@ decode_simt_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
   if (!__syncthreads_and(ok)) {
     if (threadIdx.x == 0) drain_stages(bars, last_req, C::NSTAGE, a.wait_budget);
     return;
+  }
+  // every page requested was waited for, so no copy is in flight; checked,
+  // and drained if not, before the ring is reused and the CTA exits
+  if (threadIdx.x == 0 && !stages_idle(bars, last_req, C::NSTAGE)) {
+    atomicOr(a.status, kStatusLateCopy);
+    drain_stages(bars, last_req, C::NSTAGE, a.wait_budget);
   }
 
   // ---- reduce the warp's position slots --------------------------------
@@ -487,6 +496,13 @@ static Plan plan(DecodeArgs &a, const DecodeBatch &batch) {
     if (pages > max_pages) max_pages = pages;
   }
   p.items = a.n_caches * a.n_layers * a.geom.n_heads * (G / p.gc);
+  if (a.fix_split_pages > 0 && a.fix_n_splits > 0) {
+    // a chunk of a batch planned as a whole: the same split boundaries, so
+    // every row's result equals the single launch's bit for bit
+    a.split_pages = a.fix_split_pages;
+    a.n_splits = a.fix_n_splits;
+    return p;
+  }
   const int resident = p.mma_gh ? mma_resident(p.mma_gh, a.head_dim)
                                 : (a.head_dim == 128 ? resident_gc<128>(p.gc) : resident_gc<64>(p.gc));
   int ns = 1;
@@ -509,6 +525,14 @@ static Plan plan(DecodeArgs &a, const DecodeBatch &batch) {
   a.split_pages = max_pages > 0 ? (max_pages + ns - 1) / ns : 1;
   a.n_splits = max_pages > 0 ? (max_pages + a.split_pages - 1) / a.split_pages : 1;
   return p;
+}
+
+void decode_fix_plan(DecodeArgs &a, const DecodeBatch &batch) {
+  DecodeArgs t = a;
+  t.fix_split_pages = t.fix_n_splits = 0;
+  plan(t, batch);
+  a.fix_split_pages = t.split_pages;
+  a.fix_n_splits = t.n_splits;
 }
 
 size_t decode_workspace_bytes(const DecodeArgs &a0, const DecodeBatch &batch) {

@@ -3,6 +3,7 @@
 // small math helpers.
 #pragma once
 #include "internal.cuh"
+#include "pipeline.cuh"
 
 namespace eakv {
 
@@ -39,6 +40,28 @@ __device__ __forceinline__ Item decode_item(const DecodeArgs &a, const DecodeBat
   int pg1 = min(P1, it.pg0 + a.split_pages);
   it.npages = pg1 > it.pg0 ? pg1 - it.pg0 : 0;
   return it;
+}
+
+// Self-checks of a CTA's launch arguments and work item. A CTA that fails
+// one records kStatusBadIndex in the device status word and returns before
+// it touches any memory: no split plan (division by zero in decode_item),
+// or an item that would address outside its cache's slab, the query rows
+// or the output rows.
+__device__ __forceinline__ bool launch_ok(const DecodeArgs &a) {
+  const bool ok = a.n_splits >= 1 && a.split_pages >= 1 && a.n_layers >= 1 && a.n_caches >= 1 &&
+                  a.geom.n_heads >= 1 && a.n_q_heads >= a.geom.n_heads;
+  if (!ok && threadIdx.x == 0 && a.status) atomicOr(a.status, kStatusBadIndex);
+  return ok;
+}
+
+__device__ __forceinline__ bool item_ok(const DecodeArgs &a, const Item &it, int q_head0,
+                                        int cta_heads) {
+  const bool ok = it.b >= 0 && it.b < a.n_caches && it.b < kMaxBatch && it.layer >= 0 &&
+                  it.layer < a.geom.n_layers && it.h >= 0 && it.h < a.geom.n_heads &&
+                  it.pg0 >= 0 && it.npages >= 0 && it.pg0 + it.npages <= a.geom.n_pages &&
+                  q_head0 >= 0 && q_head0 + cta_heads <= a.n_q_heads && it.split < a.n_splits;
+  if (!ok && threadIdx.x == 0 && a.status) atomicOr(a.status, kStatusBadIndex);
+  return ok;
 }
 
 }  // namespace eakv

@@ -164,7 +164,9 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
   const int G = a.n_q_heads / a.geom.n_heads;
   const int gh = a.cta_heads;   // live query heads of this CTA (<= RH)
   const int nhg = G / gh;
+  if (!launch_ok(a) || gh < 1 || gh > RH || G % gh != 0) return;
   const Item it = decode_item(a, batch, nhg);
+  if (!item_ok(a, it, it.h * G + it.hg * gh, gh)) return;
   const size_t kv_stride = (size_t)a.geom.n_heads * a.geom.n_pages;
   const uint8_t *kpages = batch.base[it.b] + page_index(a.geom, it.layer, 0, it.h, 0) * C::PB;
   const uint8_t *vpages = kpages + kv_stride * C::PB;
@@ -187,7 +189,7 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
     const uint32_t dst = smem_u32(smem + st * C::STAGE_BYTES);
     bulk_g2s(dst, kpages + (size_t)(it.pg0 + i) * C::PB, C::PB, full);
     bulk_g2s(dst + C::PB, vpages + (size_t)(it.pg0 + i) * C::PB, C::PB, full);
-    last_req[st] = i;
+    publish_requested(&last_req[st], i);
   };
   if (threadIdx.x == 0)
     for (int i = 0; i < it.npages && i < C::NSTAGE; i++) issue(i);
@@ -453,7 +455,8 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
   const int wgrp = warp / C::WPP, wsub = warp % C::WPP;
   for (int i = wgrp; i < it.npages; i += C::NW / C::WPP) {
     const int st = i % C::NSTAGE;
-    if (!ok || !mbar_wait(smem_u32(&bars[st]), (i / C::NSTAGE) & 1, a.wait_budget)) {
+    if (!ok || !wait_requested(&last_req[st], i, a.wait_budget) ||
+        !mbar_wait(smem_u32(&bars[st]), (i / C::NSTAGE) & 1, a.wait_budget)) {
       atomicOr(a.status, kStatusWaitTimeout);
       ok = false;
       break;
@@ -479,6 +482,12 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
   if (!__syncthreads_and(ok)) {
     if (threadIdx.x == 0) drain_stages(bars, last_req, C::NSTAGE, a.wait_budget);
     return;
+  }
+  // every page requested was waited for, so no copy is in flight; checked,
+  // and drained if not, before the ring is reused and the CTA exits
+  if (threadIdx.x == 0 && !stages_idle(bars, last_req, C::NSTAGE)) {
+    atomicOr(a.status, kStatusLateCopy);
+    drain_stages(bars, last_req, C::NSTAGE, a.wait_budget);
   }
 
   // ---- per-warp totals --------------------------------------------------------

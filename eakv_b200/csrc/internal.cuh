@@ -147,6 +147,8 @@ struct DecodeArgs {
   unsigned wait_budget;             // polls per bounded wait (0: the default budget)
   int test_stall;                   // > 0: page test_stall-1 of every item is never
                                     // requested, so its wait runs out (tests only)
+  int fix_split_pages, fix_n_splits;  // > 0: keep this split plan (one chunk of a
+                                      // batch that was planned as a whole)
   // filled by the planner
   int n_splits, split_pages;
   int cta_heads;                    // tensor-core path: query heads per CTA
@@ -155,6 +157,10 @@ struct DecodeArgs {
 int decode_launch(const DecodeArgs &a, const DecodeBatch &batch, void *workspace,
                   size_t workspace_bytes, cudaStream_t s);
 size_t decode_workspace_bytes(const DecodeArgs &a, const DecodeBatch &batch);
+// Plans `a` over the whole batch and records the split plan in
+// a.fix_split_pages / a.fix_n_splits, so that chunks of it launched on their
+// own keep the same splits.
+void decode_fix_plan(DecodeArgs &a, const DecodeBatch &batch);
 int lse_combine_launch(int n_parts, int n_rows, int head_dim, const float *parts,
                        const float *lse, float *out, float *lse_out, cudaStream_t s);
 int *device_status_ptr();   // status word of the current device

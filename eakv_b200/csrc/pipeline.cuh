@@ -12,6 +12,7 @@ namespace eakv {
 constexpr uint32_t kWaitBudget = 1u << 22;   // try_wait polls before giving up
 constexpr int kStatusWaitTimeout = 1;
 constexpr int kStatusBadIndex = 2;
+constexpr int kStatusLateCopy = 4;   // a stage still had a copy in flight at the end
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -52,6 +53,39 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_
   for (uint32_t i = 0; i < budget; i++)
     if (mbar_try_wait(bar, parity)) return true;
   return false;
+}
+
+// Bounded wait until page i has been requested into its stage (last = the
+// stage's "last page requested" slot). Only then is the stage's barrier in
+// page i's phase: a consumer that waited on the phase parity earlier, while
+// the barrier was still in the phase of the page two uses back, would see
+// that older phase (same parity) as complete. Pages enter a stage in
+// increasing order and page i + nstage only after page i was consumed, so
+// the slot never passes i before this wait.
+__device__ __forceinline__ bool wait_requested(const int *last, int i, uint32_t budget) {
+  const volatile int *p = last;
+  for (uint32_t k = 0; k < budget; k++)
+    if (*p >= i) {
+      __threadfence_block();
+      return true;
+    }
+  return false;
+}
+
+// Publishes "page i requested into this stage" after the barrier arrive and
+// the copies were issued (read by wait_requested).
+__device__ __forceinline__ void publish_requested(int *last, int i) {
+  __threadfence_block();
+  *reinterpret_cast<volatile int *>(last) = i;
+}
+
+// True when no stage has a copy in flight: the phase of the last page
+// requested into every stage has completed (one non-blocking test each).
+__device__ __forceinline__ bool stages_idle(const uint64_t *bars, const int *last, int nstage) {
+  bool idle = true;
+  for (int s = 0; s < nstage; s++)
+    if (last[s] >= 0 && !mbar_try_wait(smem_u32(&bars[s]), (last[s] / nstage) & 1)) idle = false;
+  return idle;
 }
 
 // After a wait ran out: wait (bounded again) for the last copy requested

@@ -33,8 +33,10 @@ int         eakv_last_error(void);
 const char *eakv_last_error_string(void);
 
 /* Sticky device status word of the library's kernels on `device`: 0 when
- * clean, else a bitmask (1 = a pipeline wait ran out of its bound, 2 = an
- * index check failed). reset != 0 clears it. Synchronizes the device.
+ * clean, else a bitmask (1 = a pipeline wait ran out of its bound, 2 = a
+ * decode work item failed its index check and was skipped, 4 = a decode
+ * CTA found a copy still in flight at its end and drained it). reset != 0
+ * clears it. Synchronizes the device.
  * Returns the status, or a negative EAKV_ERR_* code. */
 int eakv_device_status(int device, int reset);
 
@@ -110,7 +112,11 @@ int eakv_decode_attention(const eakv_cache_t *const *caches, int n_caches,
 int eakv_decode_attention_noalloc(const eakv_cache_t *const *caches,
                                   int n_caches, const float *d_queries,
                                   int n_q_heads, float *d_output, void *stream);
-/* Same with host buffers; copies in, decodes, copies out, synchronizes. */
+/* Same with host buffers; copies in, decodes, copies out, synchronizes.
+ * From 1 MiB of queries on, the batch is cut into up to four chunks of
+ * caches (or of layers, for one cache) whose copies overlap the other
+ * chunks' decodes; every chunk keeps the whole batch's split plan, so the
+ * outputs equal eakv_decode_attention's bit for bit. */
 int eakv_decode_attention_host(const eakv_cache_t *const *caches,
                                int n_caches, const float *queries,
                                int n_q_heads, float *output, void *stream);

@@ -130,6 +130,52 @@ def test_decode_batch_ragged(gpu):
         c.free()
 
 
+@pytest.mark.parametrize("shape", ["by_cache", "by_layer"])
+@pytest.mark.parametrize("pinned", [False, True])
+def test_decode_host_pipelined(gpu, shape, pinned):
+    """At 1 MiB of queries and more, the host-buffer decode runs in chunks
+    (caches, or the layers of a single cache) whose copies overlap the
+    other chunks' decodes; every chunk keeps the whole batch's split plan,
+    so the outputs equal the device-buffer form's bit for bit."""
+    import torch
+    if shape == "by_cache":
+        lens, L, nq, nkv, hd, maxS = [1, 64, 100, 333, 257, 129], 6, 64, 8, 128, 400
+    else:
+        lens, L, nq, nkv, hd, maxS = [130], 33, 64, 8, 128, 130
+    B = len(lens)
+    assert B * L * nq * hd * 4 >= 1 << 20   # the size at which chunking starts
+    rng = np.random.default_rng(77)
+    caches, refs = [], []
+    for b in range(B):
+        data = kv_data(rng, L, nkv, lens[b], hd)
+        c = E.Cache(L, nkv, hd, maxS)
+        assert c.load_raw(data, lens[b]) == 0
+        rc = O.RefCache(L, nkv, hd, maxS)
+        rc.load_raw(data, lens[b])
+        caches.append(c)
+        refs.append(rc)
+    q = rng.standard_normal((B, L, nq, hd)).astype(np.float32)
+    do = torch.full((B, L, nq, hd), float("nan"), device=gpu)
+    E.decode_attention(caches, torch.from_numpy(q).to(gpu), nq, do)
+    caches[0].synchronize()
+    out = do.cpu().numpy()
+    if pinned:
+        qh = torch.from_numpy(q).pin_memory()
+        oh = torch.full((B, L, nq, hd), float("nan")).pin_memory()
+        E.decode_attention_host(caches, qh, nq, oh)
+        out2 = oh.numpy()
+    else:
+        out2 = np.full_like(q, np.nan)
+        E.decode_attention_host(caches, q, nq, out2)
+    np.testing.assert_array_equal(out2, out)
+    for b in range(B):
+        for l in (0, L // 2, L - 1):
+            assert_close(out2[b, l].reshape(-1), refs[b].fused(q[b, l], l, nq, nkv),
+                         what=f"cache {b} layer {l}")
+    for c in caches:
+        c.free()
+
+
 def test_partial_ranges_and_lse_combine(gpu):
     """Sequence split across (simulated) ranks: partial outputs + LSE over
     disjoint position ranges, merged by eakv_lse_combine == full attention."""
