@@ -33,7 +33,10 @@
 //   in registers with one mask+or and one f16 subtract each: placing a
 //   nibble in the low mantissa bits of 1024.0 (0x6400) and subtracting 1024
 //   gives it exactly; a high nibble is taken in place (bits 4..7), i.e.
-//   times 16, and the 1/16 is applied to the output row.
+//   times 16, and the 1/16 is applied to the output row. The nibble bytes
+//   reach the registers by one transposed ldmatrix per group and step,
+//   which already pairs two positions' bytes in one register as the f16x2
+//   fragment wants.
 // * P' = p * s_v (a probability times the V scale) is split into two f16
 //   limbs, hi = f16(x) and lo = f16(x - hi), which carry ~22 bits; the
 //   tensor core accumulates in f32. P' is prescaled by 2^-E with E the
@@ -135,6 +138,27 @@ __device__ __forceinline__ void imma16832(int (&d)[4], const uint32_t (&a)[4], u
       "{%8,%9}, {%0,%1,%2,%3};"
       : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// d = A * B with a zero accumulator given as an immediate (no registers
+// zeroed first).
+__device__ __forceinline__ void imma16832_z(int (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                            uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {0,0,0,0};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Four transposed 8x8 b16 tiles from shared memory: lane t gives the row
+// address for row t % 8 of tile t / 8 (16-byte aligned) and receives, for
+// each tile, column t / 4 of rows 2 (t % 4) and 2 (t % 4) + 1 (low, high
+// half of the register).
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
 }
 
 // Signed base-256 digit l (0..3) of x, |x| <= 2^30: x = sum_l digit_l 2^(8l)
@@ -331,12 +355,6 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
 #pragma unroll
     for (int tile = 0; tile < 2; tile++) {
       int dk[NG][C::KMT][4];
-#pragma unroll
-      for (int gg = 0; gg < NG; gg++)
-#pragma unroll
-        for (int mt = 0; mt < C::KMT; mt++)
-#pragma unroll
-          for (int r = 0; r < 4; r++) dk[gg][mt][r] = 0;
       // B fragments: lane (g, c) takes bytes 8c..8c+7 of position g's group row
       const uint8_t *row = ks_ + (p0 + 8 * tile + g) * (HD / 2) + 8 * c;
 #pragma unroll
@@ -348,7 +366,10 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
           const uint32_t b0 = w & 0x0F0F0F0Fu;   // low nibbles
           const uint32_t b1 = w & 0xF0F0F0F0u;   // high nibbles x16
 #pragma unroll
-          for (int mt = 0; mt < C::KMT; mt++) imma16832(dk[gg][mt], aq[gg][ks][mt], b0, b1);
+          for (int mt = 0; mt < C::KMT; mt++) {
+            if (ks == 0) imma16832_z(dk[gg][mt], aq[gg][ks][mt], b0, b1);
+            else imma16832(dk[gg][mt], aq[gg][ks][mt], b0, b1);
+          }
         }
       }
 #pragma unroll
@@ -424,17 +445,19 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
         b0[C::VNT - 1] = bl0;
         b1[C::VNT - 1] = bl1;
       }
-      // V nibble words of this thread's four positions, byte 4g of the group
-      const uint8_t *vrow = vs_ + 32 * gg + 4 * g;
-      const uint32_t w0 = *reinterpret_cast<const uint32_t *>(vrow + tpos[0] * (HD / 2));
-      const uint32_t w1 = *reinterpret_cast<const uint32_t *>(vrow + tpos[1] * (HD / 2));
-      const uint32_t w2 = *reinterpret_cast<const uint32_t *>(vrow + tpos[2] * (HD / 2));
-      const uint32_t w3 = *reinterpret_cast<const uint32_t *>(vrow + tpos[3] * (HD / 2));
-      const uint32_t xa01 = __byte_perm(w0, w1, 0x5410), xa23 = __byte_perm(w0, w1, 0x7632);
-      const uint32_t xb01 = __byte_perm(w2, w3, 0x5410), xb23 = __byte_perm(w2, w3, 0x7632);
+      // V nibbles of the step's 16 positions, as four transposed 8x8 b16
+      // tiles: tile 2w + blk holds positions p0 + 8 blk .. + 7 (rows) and
+      // bytes 16w .. 16w + 15 of the group (8 columns of two bytes). Lane
+      // (g, c) receives bytes 16w + 2g, 16w + 2g + 1 of positions 2c, 2c+1
+      // (blk 0) and 2c+8, 2c+9 (blk 1).
+      uint32_t x[4];
+      {
+        const int t = lane >> 3, r = lane & 7;
+        ldsm_x4_trans(x, smem_u32(vs_ + (p0 + 8 * (t & 1) + r) * (HD / 2) + 32 * gg + 16 * (t >> 1)));
+      }
 #pragma unroll
-      for (int j = 0; j < 4; j++) {   // byte j of the word -> output m-tile 4*gg + j
-        const uint32_t xa = (j < 2) ? xa01 : xa23, xb = (j < 2) ? xb01 : xb23;
+      for (int j = 0; j < 4; j++) {   // byte 16 (j/2) + 2g + (j%2) -> output m-tile 4*gg + j
+        const uint32_t xa = x[2 * (j >> 1)], xb = x[2 * (j >> 1) + 1];
         const uint32_t ya = (j & 1) ? (xa >> 8) : xa, yb = (j & 1) ? (xb >> 8) : xb;
         const uint32_t a0 = nib_pair(ya, 0x000F000Fu);   // row g: low nibble, positions 2c, 2c+1
         const uint32_t a1 = nib_pair(ya, 0x00F000F0u);   // row g+8: high nibble x16
@@ -529,7 +552,7 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
       const int gg = mv >> 2, j = mv & 3;
       // undo the 2^(127 - vexp) applied to P': multiply by 2^(vexp - 127)
       const float vs = __uint_as_float((uint32_t)vexp << 23);
-      const int dlo = 64 * gg + 4 * g + j, dhi = dlo + 32;
+      const int dlo = 64 * gg + 16 * (j >> 1) + 2 * g + (j & 1), dhi = dlo + 32;
 #pragma unroll
       for (int e = 0; e < 2; e++) {
         const int h = hcol[e];
