@@ -413,6 +413,45 @@ def run_b200(args, cfg, world, rank, local):
         step(qs[i % 4], out)
     torch.cuda.synchronize()
     barrier()
+
+    # Latency-bound steps (the small configs) replay CUDA graphs of the same
+    # library calls: one graph of the per-step append (positions are the same
+    # every step: each step restores the cache to S_full - 1 first) and one
+    # decode graph per query buffer. The cache's host-side length is kept in
+    # step with restore/advance outside the graphs.
+    use_graph = (args.graph == "on" or (args.graph == "auto" and needs_flush(cfg))) and not split
+    if use_graph:
+        g_dec, g_app = [], None
+        if appending:
+            for c in caches:
+                c.restore(S_full - 1)
+            g_app = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g_app, stream=stream, capture_error_mode="thread_local"):
+                for c in caches:
+                    c.append_step_device(new_kv, 1)
+            for c in caches:
+                c.advance(1)
+        for k in range(4):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream, capture_error_mode="thread_local"):
+                E.decode_attention(caches, qs[k], nq, out, stream=sh)
+            g_dec.append(g)
+
+        def step(q_in, o, mid=None):   # noqa: F811 (graph replay of the step above)
+            if appending:
+                for c in caches:
+                    c.restore(S_full - 1)
+                g_app.replay()
+                for c in caches:
+                    c.advance(1)
+                if mid is not None:
+                    mid.record(stream)
+            g_dec[next(k for k in range(4) if qs[k] is q_in)].replay()
+
+        for i in range(args.warmup):
+            step(qs[i % 4], out)
+        torch.cuda.synchronize()
+        barrier()
     clocks = ClockSampler(local)
     clocks.start()
     mark = clocks.mark()
@@ -529,7 +568,9 @@ def run_b200(args, cfg, world, rank, local):
             "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded torch.randn K/V on device, per-channel log-uniform[0.5,8] "
                     "K scale, 4-slice pool rotated over caches/layers)",
-            "config": config_json(cfg, world, args.seq_shards),
+            "config": dict(config_json(cfg, world, args.seq_shards),
+                           step_launch=("CUDA graph replay of the library calls" if use_graph
+                                        else "direct library calls")),
             "e2e": {"value": tokens_step / (e2e_ms / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": int(qh.nbytes) + (int(kv_host.numel()) * 4
                                                             if appending else 0),
@@ -758,6 +799,9 @@ def main():
     ap.add_argument("--seq-shards", type=int, default=0,
                     help="sharded configs: ranks per sequence split (0: as many KV-head "
                          "shards as divide the ranks, the rest split the sequence)")
+    ap.add_argument("--graph", default="auto", choices=["auto", "on", "off"],
+                    help="replay the device step from CUDA graphs (auto: for the small, "
+                         "launch-latency-bound configs that flush L2 between steps)")
     ap.add_argument("--splits", type=int, default=0,
                     help="force this many sequence splits per row (0: planner's choice)")
     args = ap.parse_args()
