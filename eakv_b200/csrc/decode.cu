@@ -472,9 +472,8 @@ int resident_gc(int gc) {
 
 }  // namespace
 
-// Chooses the kernel (tensor cores for GQA groups of 4 or 8 query heads per
-// KV head, CUDA cores otherwise) and the split count: enough CTAs for ~8
-// waves of resident blocks, at least one page per split.
+// Chooses the kernel (the tensor-core kernel for head_dim 64 and 128, the
+// CUDA-core kernel when forced) and the split count.
 struct Plan {
   int mma_gh;   // 0: CUDA-core kernel
   int gc;       // query heads per CTA
@@ -482,6 +481,40 @@ struct Plan {
 };
 
 constexpr int kMaxSplitPages = 256;   // 16384 positions
+
+// Modeled duration, in page times of one CTA, of a launch of `items` rows cut
+// into splits of `sp` pages (n per row), `per_sm` CTAs resident per SM on
+// `sms` SMs. Every CTA costs its pages plus a fixed kCtaOverheadPages (query
+// set-up, pipeline fill, merge, its share of the split merge). The busiest
+// SM receives m = ceil(CTAs / sms) of them and runs them in rounds of
+// per_sm; a last round of r < per_sm CTAs costs (r / per_sm)^(2/3) of a full
+// one (its CTAs share the SM with fewer others and run faster, but not in
+// proportion). Fitted to split sweeps on the cfg1-cfg5 shapes (one row of
+// 512 pages at 4 splits: 258 us, at 2: 276 us, at 3: 296 us; cfg2 at 4: 21.7
+// us, at 16: 35.0 us), whose ranking it reproduces.
+constexpr double kCtaOverheadPages = 8.0;
+
+static double split_cost(long long items, int max_pages, int ns, int per_sm, int sms) {
+  const int sp = (max_pages + ns - 1) / ns;
+  const int n = (max_pages + sp - 1) / sp;
+  const long long m = (items * n + sms - 1) / sms;
+  const long long rounds = (m + per_sm - 1) / per_sm;
+  const long long r = m - (long long)per_sm * (rounds - 1);
+  return (sp + kCtaOverheadPages) * ((double)(rounds - 1) + pow((double)r / per_sm, 2.0 / 3.0));
+}
+
+static int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int d = dev & 63;
+  if (!cached[d]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[d] = n > 0 ? n : 148;
+  }
+  return cached[d];
+}
 
 static Plan plan(DecodeArgs &a, const DecodeBatch &batch) {
   const int G = a.n_q_heads / a.geom.n_heads;
@@ -507,17 +540,27 @@ static Plan plan(DecodeArgs &a, const DecodeBatch &batch) {
                                 : (a.head_dim == 128 ? resident_gc<128>(p.gc) : resident_gc<64>(p.gc));
   int ns = 1;
   if (max_pages > 1) {
-    long long target = 8LL * resident;
-    ns = (int)((target + p.items - 1) / p.items);
-    // the tensor-core kernel works on two pages at a time (two warps per
-    // page): a split of one page would leave half its warps idle
-    if (p.mma_gh && ns > max_pages / 2) ns = max_pages / 2 > 0 ? max_pages / 2 : 1;
-    // ... and its f32 tensor-core accumulators drift with the number of
-    // accumulation steps (1.1e-4 absolute after 512 pages of one row, on
-    // outputs of ~0.02; about half that at 256): no split is longer than
-    // kMaxSplitPages pages
-    if (p.mma_gh && ns < (max_pages + kMaxSplitPages - 1) / kMaxSplitPages)
-      ns = (max_pages + kMaxSplitPages - 1) / kMaxSplitPages;
+    // fewest splits: the tensor core's f32 accumulators drift with the
+    // number of accumulation steps (1.1e-4 absolute after 512 pages of one
+    // row, on outputs of ~0.02; about half that at 256), so no split of the
+    // tensor-core kernel is longer than kMaxSplitPages pages
+    const int lo = p.mma_gh ? (max_pages + kMaxSplitPages - 1) / kMaxSplitPages : 1;
+    // most splits: for the tensor-core kernel at least two pages per split
+    // (it gives each page to one warp, so a one-page split idles the rest)
+    int hi = p.mma_gh ? max_pages / 2 : max_pages;
+    if (hi < lo) hi = lo;
+    if (hi > 4096) hi = 4096;
+    const int sms = sm_count();
+    const int per_sm = resident / sms > 0 ? resident / sms : 1;
+    ns = lo;
+    double best = split_cost(p.items, max_pages, lo, per_sm, sms);
+    for (int k = lo + 1; k <= hi; k++) {
+      const double c = split_cost(p.items, max_pages, k, per_sm, sms);
+      if (c < best) {
+        best = c;
+        ns = k;
+      }
+    }
     if (a.force_splits > 0) ns = a.force_splits;
     if (ns > max_pages) ns = max_pages;
     if (ns < 1) ns = 1;
