@@ -73,6 +73,8 @@ struct MCfg {
   // the 4 warps of a CTA pages i, i+1, i+2, i+3 in turn
   static constexpr int WPP = 1;
   static constexpr int THREADS = NW * 32;
+  // unroll the steps of a whole page (registers allow it except at 8 heads, d128)
+  static constexpr bool UNROLL = !(HD == 128 && RH == 8);
   // CTAs per SM the register budget is cut for (128 registers at 4)
   static constexpr int MINB = (HD == 128 && RH == 8) ? 3 : 4;
   static constexpr int NIB = kPagePositions * NG * 32;
@@ -487,13 +489,24 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
     const uint8_t *ks_ = smem + st * C::STAGE_BYTES;
     const int page_pos0 = (it.pg0 + i) * kPagePositions;
     const bool full = page_pos0 >= it.r0 && page_pos0 + kPagePositions <= it.r1;
+    constexpr int STEPS = kPagePositions / (16 * C::WPP);
+    if (full) {
+      // a whole page: its steps unrolled, so their shared-memory addresses
+      // are immediate offsets from the stage (not for the 8-head d128
+      // kernel, which would spill)
+      if constexpr (C::UNROLL) {
+#pragma unroll
+        for (int s2 = 0; s2 < STEPS; s2++)
+          page_body(std::true_type{}, ks_, page_pos0, (kPagePositions / C::WPP) * wsub + 16 * s2);
+      } else {
 #pragma unroll 1
-    for (int s2 = 0; s2 < kPagePositions / (16 * C::WPP); s2++) {
-      const int p0 = (kPagePositions / C::WPP) * wsub + 16 * s2;
-      if (full)
-        page_body(std::true_type{}, ks_, page_pos0, p0);
-      else
-        page_body(std::false_type{}, ks_, page_pos0, p0);
+        for (int s2 = 0; s2 < STEPS; s2++)
+          page_body(std::true_type{}, ks_, page_pos0, (kPagePositions / C::WPP) * wsub + 16 * s2);
+      }
+    } else {
+#pragma unroll 1
+      for (int s2 = 0; s2 < STEPS; s2++)
+        page_body(std::false_type{}, ks_, page_pos0, (kPagePositions / C::WPP) * wsub + 16 * s2);
     }
     __syncwarp();
     // the last warp of the group to finish with this stage refills it with
