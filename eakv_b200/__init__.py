@@ -79,6 +79,7 @@ SIGNATURES = {
     "eakv_lse_combine": (_I, [_I, _I, _I, _P, _P, _P, _P, _P]),
     "eakv_test_force_splits": (_I, [_I]),
     "eakv_test_force_path": (_I, [_I]),
+    "eakv_test_choose_splits": (_I, [_c.c_longlong, _I, _I, _I, _I, _I]),
     "eakv_test_stall": (_I, [_I, ctypes.c_uint]),
     "eakv_cache_validate": (_I, [_P, _P]),
     "eakv_cache_dequantize_device": (_I, [_P, _I, _I, _I, _I, _P, _P]),
@@ -377,6 +378,14 @@ def device_status(device=0, reset=False):
 
 def force_splits(n):
     lib().eakv_test_force_splits(int(n))
+
+
+def choose_splits(items, max_pages, lo, hi, per_sm, sms):
+    """The decode planner's split count for `items` rows of max_pages pages,
+    searched in [lo, hi], with per_sm CTAs resident on each of `sms` SMs
+    (host code only: runs without a GPU)."""
+    return lib().eakv_test_choose_splits(int(items), int(max_pages), int(lo), int(hi),
+                                         int(per_sm), int(sms))
 
 
 def force_path(path):

@@ -460,6 +460,11 @@ int eakv_lse_combine(int n_parts, int n_rows, int head_dim, const float *d_parts
 
 }  // extern "C"
 
+extern "C" int eakv_test_choose_splits(long long items, int max_pages, int lo, int hi,
+                                       int per_sm, int sms) {
+  return eakv::choose_splits(items, max_pages, lo, hi, per_sm, sms);
+}
+
 extern "C" int eakv_test_force_path(int path) {
   eakv::t_force_path = path == 1 ? 1 : 0;
   return EAKV_OK;

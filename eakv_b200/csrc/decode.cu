@@ -503,6 +503,21 @@ static double split_cost(long long items, int max_pages, int ns, int per_sm, int
   return (sp + kCtaOverheadPages) * ((double)(rounds - 1) + pow((double)r / per_sm, 2.0 / 3.0));
 }
 
+// The split count in [lo, hi] of least modeled duration (the first of equals).
+int choose_splits(long long items, int max_pages, int lo, int hi, int per_sm, int sms) {
+  if (max_pages < 1 || lo < 1 || hi < lo || per_sm < 1 || sms < 1) return lo > 0 ? lo : 1;
+  int ns = lo;
+  double best = split_cost(items, max_pages, lo, per_sm, sms);
+  for (int k = lo + 1; k <= hi; k++) {
+    const double c = split_cost(items, max_pages, k, per_sm, sms);
+    if (c < best) {
+      best = c;
+      ns = k;
+    }
+  }
+  return ns;
+}
+
 static int sm_count() {
   static int cached[64] = {0};
   int dev = 0;
@@ -552,15 +567,7 @@ static Plan plan(DecodeArgs &a, const DecodeBatch &batch) {
     if (hi > 4096) hi = 4096;
     const int sms = sm_count();
     const int per_sm = resident / sms > 0 ? resident / sms : 1;
-    ns = lo;
-    double best = split_cost(p.items, max_pages, lo, per_sm, sms);
-    for (int k = lo + 1; k <= hi; k++) {
-      const double c = split_cost(p.items, max_pages, k, per_sm, sms);
-      if (c < best) {
-        best = c;
-        ns = k;
-      }
-    }
+    ns = choose_splits(p.items, max_pages, lo, hi, per_sm, sms);
     if (a.force_splits > 0) ns = a.force_splits;
     if (ns > max_pages) ns = max_pages;
     if (ns < 1) ns = 1;

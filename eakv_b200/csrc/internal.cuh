@@ -161,6 +161,9 @@ size_t decode_workspace_bytes(const DecodeArgs &a, const DecodeBatch &batch);
 // a.fix_split_pages / a.fix_n_splits, so that chunks of it launched on their
 // own keep the same splits.
 void decode_fix_plan(DecodeArgs &a, const DecodeBatch &batch);
+// The planner's split count for `items` rows of max_pages pages, searched in
+// [lo, hi], per_sm CTAs resident on each of `sms` SMs (host code only).
+int choose_splits(long long items, int max_pages, int lo, int hi, int per_sm, int sms);
 int lse_combine_launch(int n_parts, int n_rows, int head_dim, const float *parts,
                        const float *lse, float *out, float *lse_out, cudaStream_t s);
 int *device_status_ptr();   // status word of the current device

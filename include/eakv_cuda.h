@@ -174,6 +174,14 @@ int eakv_cache_dequantize(const eakv_cache_t *cache, int layer, int kv_idx, int 
  * can exercise the split + combine path on small caches. */
 int eakv_test_force_splits(int n);
 
+/* The decode planner's split count, for tests of the planner without a GPU
+ * (pure host code, no CUDA call): `items` rows of max_pages pages, searched
+ * in [lo, hi], per_sm CTAs resident on each of `sms` SMs. The planner itself
+ * takes lo and hi from the precision cap and the two-page minimum, and
+ * per_sm / sms from the device. */
+int eakv_test_choose_splits(long long items, int max_pages, int lo, int hi, int per_sm,
+                            int sms);
+
 /* path 1 makes later fused / decode calls on this host thread use the
  * CUDA-core kernel even for shapes the tensor-core kernel serves (GQA
  * groups of 4 or 8); 0 restores the automatic choice. For tests and
