@@ -381,7 +381,7 @@ def run_b200(args, cfg, world, rank, local):
         new_kv = torch.randn(L, 2, lcfg["nkv"], 1, hd, device=dev)
         for c in caches:
             c.set_stream(sh)
-        launches_per_step += 2   # the append of every layer and K/V + its V-exponent kernel
+        launches_per_step += 1   # the append of every layer and K/V (one launch)
 
     def step(q_in, o, mid=None):
         if appending:

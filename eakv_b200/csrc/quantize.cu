@@ -13,26 +13,28 @@
 //   * between -0.0 and +0.0 the first one in element order wins, so when
 //     the min (or max) is a zero the kernel looks up the first zero.
 //
-// Mapping: 4 threads per 64-float group. Thread j loads elements 8j..8j+7
-// (the low nibbles of bytes 8j..8j+7) and 32+8j..32+8j+7 (their high
-// nibbles) as four 16-byte loads, and stores the 8 packed bytes as one
-// 8-byte word, so a warp moves 8 groups with fully coalesced traffic and
+// Mapping: 2 threads per 64-float group. Thread j loads elements 16j..16j+15
+// (the low nibbles of bytes 16j..16j+15) and 32+16j..32+16j+15 (their high
+// nibbles) as eight 16-byte loads, and stores the 16 packed bytes as one
+// 16-byte word, so a warp moves 16 groups with fully coalesced traffic and
 // the per-group work (min/max reduction, the two divisions) is shared by
-// 8 groups per warp instruction.
+// 16 groups per warp instruction (4 threads per group measured 37.2 us per
+// cfg4 append slice, 2 threads 35.1 us).
 // HBM-bound: 256 B read + 40 B written per group.
 //
 // The cache keeps, per (layer, KV head), the largest biased exponent of any
-// V scale (the decode kernels scale probabilities by it). A second, small
-// kernel raises that table from the scales just written: 8 B read per V
-// group and one atomicMax per block, so the quantize loop itself carries
-// no bookkeeping.
+// V scale (the decode kernels scale probabilities by it). The same kernel
+// raises it: a warp whose groups all belong to one (layer, V, head) unit
+// reduces their exponents and one lane raises the table (a load, and an
+// atomicMax only when the table holds less). A separate kernel over the
+// scales just written cost 8 us per V slice, a launch of its own.
 #include "internal.cuh"
 
 namespace eakv {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kTPG = 4;   // threads per 64-element group
+constexpr int kTPG = 2;   // threads per 64-element group
 
 // The reference truncates with x86 cvttss2si, which returns INT_MIN for NaN
 // and for anything outside the int32 range; the clamp then gives 0. That
@@ -147,6 +149,32 @@ quantize_kernel(const float *__restrict__ src, uint8_t *__restrict__ dst, PageGe
       scale = __fdiv_rn(range, 15.0f);
       inv = __fdiv_rn(15.0f, range);
     }
+    // V slices: raise the cache's per-(layer, head) maximum V-scale
+    // exponent. A warp's groups nearly always belong to one unit: then its
+    // largest exponent is raised by one lane, with an atomic only when the
+    // table holds less; at a unit boundary each group raises its own.
+    {
+      const long long U = unit_base + u;
+      const int lkv = (int)(U / g.n_heads);
+      const bool isv = valid && (lkv & 1);
+      const unsigned vmask = __ballot_sync(0xffffffffu, isv);
+      if (vmask) {
+        const int ex = isv ? (int)((__float_as_uint(scale) >> 23) & 0xFF) : 0;
+        const int lead = __ffs(vmask) - 1;
+        const long long Ul = __shfl_sync(0xffffffffu, U, lead);
+        if (__all_sync(0xffffffffu, !isv || U == Ul)) {
+          const int m = __reduce_max_sync(0xffffffffu, ex);
+          if (lane == lead) {
+            const int lv = (int)(Ul / g.n_heads);
+            int *p = vexp_table(dst, g) + (lv >> 1) * g.n_heads + (int)(Ul - (long long)lv * g.n_heads);
+            if (m > *reinterpret_cast<volatile int *>(p)) atomicMax(p, m);
+          }
+        } else if (isv && j == 0) {
+          int *p = vexp_table(dst, g) + (lkv >> 1) * g.n_heads + (int)(U - (long long)lkv * g.n_heads);
+          if (ex > *reinterpret_cast<volatile int *>(p)) atomicMax(p, ex);
+        }
+      }
+    }
     uint32_t word[EPT / 4];
 #pragma unroll
     for (int w = 0; w < EPT / 4; w++) {
@@ -167,44 +195,15 @@ quantize_kernel(const float *__restrict__ src, uint8_t *__restrict__ dst, PageGe
       uint8_t *pp = dst + ((size_t)(unit_base + u) * g.n_pages + page) * g.page_bytes;
       const int slot = pip * g.gpd + grp;
       uint8_t *wp = pp + (size_t)slot * 32 + EPT * j;
-      if (EPT == 8)
+      if constexpr (EPT == 16)
+        *reinterpret_cast<uint4 *>(wp) = make_uint4(word[0], word[1], word[2], word[3]);
+      else if constexpr (EPT == 8)
         *reinterpret_cast<uint2 *>(wp) = make_uint2(word[0], word[EPT / 4 - 1]);
       else
         *reinterpret_cast<uint32_t *>(wp) = word[0];
       if (j == 0)
         *reinterpret_cast<float2 *>(pp + g.nib_bytes + (size_t)slot * 8) = make_float2(scale, mn);
     }
-  }
-}
-
-// Raises the cache's V-scale exponent table over the groups just written:
-// block (x, y) takes chunk x of unit unit_base + y (K units return at once),
-// reduces the biased exponents of its scales and makes one atomicMax.
-__global__ void __launch_bounds__(kThreads)
-vexp_kernel(uint8_t *__restrict__ dst, PageGeom g, int unit_base, int n_tok, int pos0) {
-  const int U = unit_base + (int)blockIdx.y;   // (layer * 2 + kv) * heads + head
-  const int lkv = U / g.n_heads;
-  if (!(lkv & 1)) return;
-  const long long per_unit = (long long)n_tok * g.gpd;
-  int e = 0;
-  for (long long gi = (long long)blockIdx.x * kThreads + threadIdx.x; gi < per_unit;
-       gi += (long long)gridDim.x * kThreads) {
-    const int t = (int)(gi / g.gpd);
-    const int grp = (int)(gi - (long long)t * g.gpd);
-    const int pos = pos0 + t;
-    const int page = pos / kPagePositions;
-    const uint8_t *pp = dst + ((size_t)U * g.n_pages + page) * g.page_bytes;
-    const float scale = reinterpret_cast<const float2 *>(pp + g.nib_bytes)
-                            [(pos - page * kPagePositions) * g.gpd + grp].x;
-    e = max(e, (int)((__float_as_uint(scale) >> 23) & 0xFF));
-  }
-  e = __reduce_max_sync(0xffffffffu, e);
-  __shared__ int wmax[kThreads / 32];
-  if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = e;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int w = 1; w < kThreads / 32; w++) e = max(e, wmax[w]);
-    atomicMax(vexp_table(dst, g) + (lkv >> 1) * g.n_heads + (U - lkv * g.n_heads), e);
   }
 }
 
@@ -228,19 +227,6 @@ cudaError_t launch_quantize(const PageGeom &g, uint8_t *d_buf, const float *d_sr
   else
     quantize_kernel<false><<<(int)blocks, kThreads, 0, s>>>(d_src, d_buf, g, unit_base, n_groups,
                                                             n_tok, pos0, head_dim);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  // V units in the range: keep the per-(layer, head) max V-scale exponent
-  const int first_v = (unit_base / g.n_heads) | 1;   // first (layer, V) slice at or after
-  if (first_v * g.n_heads >= unit_base + n_units && (unit_base / g.n_heads) % 2 == 0) return cudaSuccess;
-  const long long per_unit = (long long)n_tok * g.gpd;
-  long long chunks = (per_unit + 8LL * kThreads - 1) / (8LL * kThreads);   // ~8 groups a thread
-  if (chunks > 65535) chunks = 65535;
-  for (int y0 = 0; y0 < n_units; y0 += 65535) {
-    const int ny = n_units - y0 < 65535 ? n_units - y0 : 65535;
-    vexp_kernel<<<dim3((unsigned)chunks, (unsigned)ny), kThreads, 0, s>>>(d_buf, g, unit_base + y0,
-                                                                         n_tok, pos0);
-  }
   return cudaGetLastError();
 }
 
