@@ -48,8 +48,10 @@ __device__ __forceinline__ int quant_one(float x, float mn, float inv) {
   return q < 0 ? 0 : (q > 15 ? 15 : q);
 }
 
+// 4 blocks per SM (at most 64 registers, no spill): 33.0 us per cfg4 append
+// slice against 35.0 at 3 blocks (79 registers); 5 blocks spill (36 us).
 template <bool kVec>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 4)
 quantize_kernel(const float *__restrict__ src, uint8_t *__restrict__ dst, PageGeom g,
                 int unit_base, long long n_groups, int n_tok, int pos0, int head_dim) {
   constexpr int EPT = 32 / kTPG;          // elements per thread in each half of the group
