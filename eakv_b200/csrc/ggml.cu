@@ -64,41 +64,61 @@ __device__ __forceinline__ float2 load_dm(const uint8_t *blk) {
                      *reinterpret_cast<const float *>(blk + 36));
 }
 
+// Each half warp takes kQB consecutive blocks per trip and loads all of them
+// before it works on any (more loads in flight per warp); the arithmetic of
+// a block is unchanged.
+constexpr int kQB = 4;
+
 __global__ void __launch_bounds__(kThreads)
 ggml_quantize_kernel(const float *__restrict__ src, uint8_t *__restrict__ dst, long long nb) {
   const int l = threadIdx.x & 15;
   const unsigned hm = half_mask();
   const long long halves = (long long)gridDim.x * (kThreads / 16);
-  for (long long i = (long long)blockIdx.x * (kThreads / 16) + (threadIdx.x >> 4); i < nb;
-       i += halves) {
-    const float *x = src + i * 64;
-    const float x0 = x[l], x1 = x[16 + l], x2 = x[32 + l], x3 = x[48 + l];
-    float vmin = x0, vmax = x0;
-    vmin = minps(vmin, x1);
-    vmax = maxps(vmax, x1);
-    vmin = minps(vmin, x2);
-    vmax = maxps(vmax, x2);
-    vmin = minps(vmin, x3);
-    vmax = maxps(vmax, x3);
-    const float mn = reduce16<false>(vmin, l, hm);
-    const float mx = reduce16<true>(vmax, l, hm);
-    const float range = __fsub_rn(mx, mn);
-    const float d = __fdiv_rn(range, 15.0f);
-    const float id = range > 0.0f ? __fdiv_rn(15.0f, range) : 0.0f;
-    // after the clamp t is in [0, 15] or NaN; cvtt(t) is then floor(t), the
-    // low 4 bits of t + 2^23 added toward zero, or for NaN INT32_MIN, whose
-    // low byte and whose value shifted left by 4 are both 0
-    auto q = [&](float v) {
-      float t = __fmul_rn(__fsub_rn(v, mn), id);
-      t = minps(15.0f, maxps(0.0f, __fadd_rn(t, 0.5f)));
-      return t == t ? ((unsigned)__float_as_int(__fadd_rz(t, 8388608.0f)) & 15u) : 0u;
-    };
-    uint8_t *blk = dst + i * kBlockBytes;
-    blk[l] = (uint8_t)((q(x0) | (q(x2) << 4)) & 0xFF);
-    blk[16 + l] = (uint8_t)((q(x1) | (q(x3) << 4)) & 0xFF);
-    if (l == 0) {
-      *reinterpret_cast<float *>(blk + 32) = d;
-      *reinterpret_cast<float *>(blk + 36) = mn;
+  for (long long i0 = ((long long)blockIdx.x * (kThreads / 16) + (threadIdx.x >> 4)) * kQB; i0 < nb;
+       i0 += halves * kQB) {
+    float xs[kQB][4];
+#pragma unroll
+    for (int k = 0; k < kQB; k++) {
+      if (i0 + k < nb) {
+        const float *x = src + (i0 + k) * 64;
+        xs[k][0] = x[l];
+        xs[k][1] = x[16 + l];
+        xs[k][2] = x[32 + l];
+        xs[k][3] = x[48 + l];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kQB; k++) {
+      if (i0 + k >= nb) break;   // uniform over the half warp
+      const long long i = i0 + k;
+      const float x0 = xs[k][0], x1 = xs[k][1], x2 = xs[k][2], x3 = xs[k][3];
+      float vmin = x0, vmax = x0;
+      vmin = minps(vmin, x1);
+      vmax = maxps(vmax, x1);
+      vmin = minps(vmin, x2);
+      vmax = maxps(vmax, x2);
+      vmin = minps(vmin, x3);
+      vmax = maxps(vmax, x3);
+      const float mn = reduce16<false>(vmin, l, hm);
+      const float mx = reduce16<true>(vmax, l, hm);
+      const float range = __fsub_rn(mx, mn);
+      const float d = __fdiv_rn(range, 15.0f);
+      const float id = range > 0.0f ? __fdiv_rn(15.0f, range) : 0.0f;
+      // after the clamp t is in [0, 15] or NaN; cvtt(t) is then floor(t), the
+      // low 4 bits of t + 2^23 added toward zero, or for NaN INT32_MIN, whose
+      // low byte and whose value shifted left by 4 are both 0
+      auto q = [&](float v) {
+        float t = __fmul_rn(__fsub_rn(v, mn), id);
+        t = minps(15.0f, maxps(0.0f, __fadd_rn(t, 0.5f)));
+        return t == t ? ((unsigned)__float_as_int(__fadd_rz(t, 8388608.0f)) & 15u) : 0u;
+      };
+      uint8_t *blk = dst + i * kBlockBytes;
+      blk[l] = (uint8_t)((q(x0) | (q(x2) << 4)) & 0xFF);
+      blk[16 + l] = (uint8_t)((q(x1) | (q(x3) << 4)) & 0xFF);
+      if (l == 0) {
+        *reinterpret_cast<float *>(blk + 32) = d;
+        *reinterpret_cast<float *>(blk + 36) = mn;
+      }
     }
   }
 }
