@@ -4,6 +4,7 @@
 #include <math.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "internal.cuh"
@@ -22,19 +23,21 @@ thread_local int t_test_stall = 0;
 thread_local unsigned t_wait_budget = 0;
 
 int *device_status_ptr() {
-  static int *ptrs[64] = {nullptr};
+  static std::atomic<int *> ptrs[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return nullptr;
-  if (!ptrs[dev]) {
-    void *p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_status) != cudaSuccess) {
+  int *p = ptrs[dev].load(std::memory_order_acquire);
+  if (!p) {
+    void *q = nullptr;
+    if (cudaGetSymbolAddress(&q, g_status) != cudaSuccess) {
       cudaGetLastError();
       return nullptr;
     }
-    ptrs[dev] = (int *)p;
+    p = (int *)q;
+    ptrs[dev].store(p, std::memory_order_release);
   }
-  return ptrs[dev];
+  return p;
 }
 
 }  // namespace eakv

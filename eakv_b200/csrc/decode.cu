@@ -23,6 +23,8 @@
 #include <math.h>
 #include <stdio.h>
 
+#include <atomic>
+
 #include "internal.cuh"
 #include "pipeline.cuh"
 #include "decode_common.cuh"
@@ -414,13 +416,13 @@ template <int HD, int GC>
 int launch_simt(const DecodeArgs &a, const DecodeBatch &b, int n_blocks, cudaStream_t s) {
   using C = Cfg<HD, GC>;
   auto fn = decode_simt_kernel<HD, GC>;
-  static unsigned long long attr_done = 0;   // one bit per device
+  static std::atomic<unsigned long long> attr_done{0};   // one bit per device
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(attr_done >> (dev & 63) & 1)) {
+  if (!(attr_done.load(std::memory_order_acquire) >> (dev & 63) & 1)) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return check_cuda(e, "decode: smem attribute");
-    attr_done |= 1ull << (dev & 63);
+    attr_done.fetch_or(1ull << (dev & 63), std::memory_order_acq_rel);
   }
   fn<<<n_blocks, C::THREADS, C::SMEM, s>>>(a, b);
   return check_cuda(cudaGetLastError(), "decode launch");
@@ -429,18 +431,21 @@ int launch_simt(const DecodeArgs &a, const DecodeBatch &b, int n_blocks, cudaStr
 template <int HD, int GC>
 int resident_simt() {
   using C = Cfg<HD, GC>;
-  static int cached = 0;
-  if (cached) return cached;
+  // per device (resident CTAs per SM x SMs), filled on first use
+  static std::atomic<int> cached[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int hit = cached[dev & 63].load(std::memory_order_relaxed);
+  if (hit) return hit;
   cudaFuncSetAttribute(decode_simt_kernel<HD, GC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        C::SMEM);
-  int per_sm = 1, dev = 0, sms = 148;
+  int per_sm = 1, sms = 148;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_simt_kernel<HD, GC>, C::THREADS,
                                                 C::SMEM);
-  cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (per_sm < 1) per_sm = 1;
-  cached = per_sm * sms;
-  return cached;
+  cached[dev & 63].store(per_sm * sms, std::memory_order_relaxed);
+  return per_sm * sms;
 }
 
 int pick_gc(int G) {
@@ -519,16 +524,17 @@ int choose_splits(long long items, int max_pages, int lo, int hi, int per_sm, in
 }
 
 static int sm_count() {
-  static int cached[64] = {0};
+  static std::atomic<int> cached[64];
   int dev = 0;
   cudaGetDevice(&dev);
   const int d = dev & 63;
-  if (!cached[d]) {
-    int n = 0;
+  int n = cached[d].load(std::memory_order_relaxed);
+  if (!n) {
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cached[d] = n > 0 ? n : 148;
+    if (n <= 0) n = 148;
+    cached[d].store(n, std::memory_order_relaxed);
   }
-  return cached[d];
+  return n;
 }
 
 static Plan plan(DecodeArgs &a, const DecodeBatch &batch) {

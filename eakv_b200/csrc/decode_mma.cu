@@ -49,6 +49,8 @@
 #include <cuda_fp16.h>
 #include <math.h>
 
+#include <atomic>
+
 #include <type_traits>
 
 #include "internal.cuh"
@@ -610,13 +612,13 @@ template <int HD, int RH>
 int launch_one(const DecodeArgs &a, const DecodeBatch &b, int n_blocks, cudaStream_t s) {
   using C = MCfg<HD, RH>;
   auto fn = decode_mma_kernel<HD, RH>;
-  static unsigned long long attr_done = 0;
+  static std::atomic<unsigned long long> attr_done{0};   // one bit per device
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(attr_done >> (dev & 63) & 1)) {
+  if (!(attr_done.load(std::memory_order_acquire) >> (dev & 63) & 1)) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return check_cuda(e, "decode_mma: smem attribute");
-    attr_done |= 1ull << (dev & 63);
+    attr_done.fetch_or(1ull << (dev & 63), std::memory_order_acq_rel);
   }
   fn<<<n_blocks, C::THREADS, C::SMEM, s>>>(a, b);
   return check_cuda(cudaGetLastError(), "decode_mma launch");
@@ -625,17 +627,21 @@ int launch_one(const DecodeArgs &a, const DecodeBatch &b, int n_blocks, cudaStre
 template <int HD, int RH>
 int resident_one() {
   using C = MCfg<HD, RH>;
-  static int cached = 0;
-  if (cached) return cached;
+  // per device (resident CTAs per SM x SMs), filled on first use
+  static std::atomic<int> cached[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int hit = cached[dev & 63].load(std::memory_order_relaxed);
+  if (hit) return hit;
   cudaFuncSetAttribute(decode_mma_kernel<HD, RH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        C::SMEM);
-  int per_sm = 1, dev = 0, sms = 148;
+  int per_sm = 1, sms = 148;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_mma_kernel<HD, RH>, C::THREADS,
                                                 C::SMEM);
-  cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  cached = (per_sm < 1 ? 1 : per_sm) * sms;
-  return cached;
+  const int r = (per_sm < 1 ? 1 : per_sm) * sms;
+  cached[dev & 63].store(r, std::memory_order_relaxed);
+  return r;
 }
 
 }  // namespace
