@@ -64,9 +64,9 @@ __device__ __forceinline__ float2 load_dm(const uint8_t *blk) {
                      *reinterpret_cast<const float *>(blk + 36));
 }
 
-// Each half warp takes kQB consecutive blocks per trip and loads all of them
-// before it works on any (more loads in flight per warp); the arithmetic of
-// a block is unchanged.
+// from_float and to_float: each half warp takes kQB consecutive blocks per
+// trip and loads all of them before it works on any (more loads in flight
+// per warp); the arithmetic of a block is unchanged.
 constexpr int kQB = 4;
 
 __global__ void __launch_bounds__(kThreads)
@@ -127,16 +127,28 @@ __global__ void __launch_bounds__(kThreads)
 ggml_dequantize_kernel(const uint8_t *__restrict__ src, float *__restrict__ dst, long long nb) {
   const int l = threadIdx.x & 15;
   const long long halves = (long long)gridDim.x * (kThreads / 16);
-  for (long long i = (long long)blockIdx.x * (kThreads / 16) + (threadIdx.x >> 4); i < nb;
-       i += halves) {
-    const uint8_t *blk = src + i * kBlockBytes;
-    const float2 dm = load_dm(blk);
-    const uint8_t r0 = blk[l], r1 = blk[16 + l];
-    float *out = dst + i * 64;
-    out[l] = fmaf((float)(r0 & 15), dm.x, dm.y);
-    out[16 + l] = fmaf((float)(r1 & 15), dm.x, dm.y);
-    out[32 + l] = fmaf((float)(r0 >> 4), dm.x, dm.y);
-    out[48 + l] = fmaf((float)(r1 >> 4), dm.x, dm.y);
+  for (long long i0 = ((long long)blockIdx.x * (kThreads / 16) + (threadIdx.x >> 4)) * kQB; i0 < nb;
+       i0 += halves * kQB) {
+    float2 dm[kQB];
+    uint8_t r0[kQB], r1[kQB];
+#pragma unroll
+    for (int k = 0; k < kQB; k++) {
+      if (i0 + k < nb) {
+        const uint8_t *blk = src + (i0 + k) * kBlockBytes;
+        dm[k] = load_dm(blk);
+        r0[k] = blk[l];
+        r1[k] = blk[16 + l];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kQB; k++) {
+      if (i0 + k >= nb) break;
+      float *out = dst + (i0 + k) * 64;
+      out[l] = fmaf((float)(r0[k] & 15), dm[k].x, dm[k].y);
+      out[16 + l] = fmaf((float)(r1[k] & 15), dm[k].x, dm[k].y);
+      out[32 + l] = fmaf((float)(r0[k] >> 4), dm[k].x, dm[k].y);
+      out[48 + l] = fmaf((float)(r1[k] >> 4), dm[k].x, dm[k].y);
+    }
   }
 }
 
