@@ -26,50 +26,60 @@ __device__ __forceinline__ bool is_nan_bits(float v) {
   return b > 2139095040 || (b < 0 && b > -8388608);
 }
 
-// Block (x, y): pages x*kPagesPerBlock.. of every head of block y =
-// layer*2 + kv; its threads take the (head, page, slot) units in order,
-// kUnroll loads at a time.
+// Block (x, y, z): pages x*kPagesPerBlock.. of KV head z of block y =
+// layer*2 + kv. Its threads read the (scale, bias) pairs of those pages as
+// 16-byte vectors (two slots each), kUnroll loads at a time; the position
+// and group of a slot are worked out only for a failing one.
 constexpr int kPagesPerBlock = 8;
 
 __global__ void __launch_bounds__(kThreads)
 validate_kernel(const uint8_t *__restrict__ buf, PageGeom g, int seq_len,
                 unsigned long long *__restrict__ keys) {
-  constexpr int kUnroll = 4;   // loads in flight per thread
+  constexpr int kUnroll = 2;   // loads in flight per thread
   const int lkv = blockIdx.y;  // layer * 2 + kv
-  const int used_pages = (seq_len + kPagePositions - 1) / kPagePositions;
+  const int h = blockIdx.z;    // KV head
   const int pg0 = blockIdx.x * kPagesPerBlock;
+  const int used_pages = (seq_len + kPagePositions - 1) / kPagePositions;
   const int n_pg = min(kPagesPerBlock, used_pages - pg0);
-  const int slots = kPagePositions * g.gpd;
-  const int per_head = n_pg * slots;
-  const int total = g.n_heads * per_head;   // (head, page, slot) units of this block
+  const int vec = kPagePositions * g.gpd / 2;   // 16-byte vectors of (scale, bias) pairs per page
+  const int total = n_pg * vec;
+  const uint8_t *base =
+      buf + (((size_t)lkv * g.n_heads + h) * g.n_pages + pg0) * g.page_bytes + g.nib_bytes;
   unsigned long long best = ~0ull;
-  for (int u0 = threadIdx.x; u0 < total; u0 += kThreads * kUnroll) {
-    float2 sb[kUnroll];
-    int t[kUnroll], hh[kUnroll], sl[kUnroll];
+  for (int r0 = threadIdx.x; r0 < total; r0 += kThreads * kUnroll) {
+    float4 sb[kUnroll];
+    int pl[kUnroll], q[kUnroll];
 #pragma unroll
     for (int k = 0; k < kUnroll; k++) {
-      const int u = u0 + k * kThreads;
-      t[k] = seq_len;   // marks "no unit"
-      if (u < total) {
-        const int h = u / per_head, r = u - h * per_head;
-        const int pg = pg0 + r / slots, s_ = r - (r / slots) * slots;
-        const float2 *sbp = reinterpret_cast<const float2 *>(
-            buf + (((size_t)lkv * g.n_heads + h) * g.n_pages + pg) * g.page_bytes + g.nib_bytes);
-        hh[k] = h;
-        sl[k] = s_;
-        t[k] = pg * kPagePositions + s_ / g.gpd;
-        if (t[k] < seq_len) sb[k] = sbp[s_];
+      const int r = r0 + k * kThreads;
+      pl[k] = -1;
+      q[k] = 0;
+      if (r < total) {
+        pl[k] = r / vec;
+        q[k] = r - pl[k] * vec;
+        sb[k] = *reinterpret_cast<const float4 *>(base + (size_t)pl[k] * g.page_bytes + q[k] * 16);
       }
     }
 #pragma unroll
     for (int k = 0; k < kUnroll; k++) {
-      if (t[k] >= seq_len) continue;
-      const int code = is_nan_bits(sb[k].x) ? 1 : is_nan_bits(sb[k].y) ? 2 : (sb[k].x < 0.0f ? 3 : 0);
-      if (code) {
-        // dense index of the group: [head][position][group]
-        const unsigned long long gi = ((unsigned long long)hh[k] * seq_len + t[k]) * g.gpd +
-                                      (sl[k] - (sl[k] / g.gpd) * g.gpd);
-        best = min(best, gi * 4 + code);
+      if (pl[k] < 0) continue;
+      // slots 2q and 2q+1 of the page; slot s is position s / gpd, group s % gpd,
+      // and only slots of positions below seq_len count
+      const int page = pg0 + pl[k];
+      const int limit = min(kPagePositions, seq_len - page * kPagePositions) * g.gpd;
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        const int s_ = 2 * q[k] + e;
+        if (s_ >= limit) continue;
+        const float sc = e ? sb[k].z : sb[k].x, bi = e ? sb[k].w : sb[k].y;
+        const int code = is_nan_bits(sc) ? 1 : is_nan_bits(bi) ? 2 : (sc < 0.0f ? 3 : 0);
+        if (code) {
+          // dense index of the group: [head][position][group]
+          const int t = page * kPagePositions + s_ / g.gpd;
+          const unsigned long long gi =
+              ((unsigned long long)h * seq_len + t) * g.gpd + (unsigned long long)(s_ % g.gpd);
+          best = min(best, gi * 4 + code);
+        }
       }
     }
   }
@@ -148,6 +158,10 @@ int eakv_cache_validate(const eakv_cache_t *cc, int32_t *codes) {
   const int n = c->n_layers * 2;
   for (int i = 0; i < n; i++) codes[i] = 0;
   if (c->seq_len == 0 || c->geom.gpd == 0) return EAKV_OK;
+  if (n > 65535 || c->n_kv_heads > 65535) {   // grid y and z
+    set_error(EAKV_ERR_INVALID, "validate: more than 65535 (layer, K/V) blocks or KV heads");
+    return EAKV_ERR_INVALID;
+  }
   DeviceGuard g(c->device);
   unsigned long long *d_keys = (unsigned long long *)cache_scratch(c, (size_t)n * 8);
   if (!d_keys) return EAKV_ERR_ALLOC;
@@ -155,7 +169,8 @@ int eakv_cache_validate(const eakv_cache_t *cc, int32_t *codes) {
   if (rc) return rc;
   const int used_pages = (c->seq_len + kPagePositions - 1) / kPagePositions;
   const int bx = (used_pages + kPagesPerBlock - 1) / kPagesPerBlock;
-  validate_kernel<<<dim3(bx, n), kThreads, 0, c->stream>>>(c->d_buf, c->geom, c->seq_len, d_keys);
+  validate_kernel<<<dim3(bx, n, c->n_kv_heads), kThreads, 0, c->stream>>>(c->d_buf, c->geom,
+                                                                          c->seq_len, d_keys);
   rc = check_cuda(cudaGetLastError(), "validate: launch");
   if (rc) return rc;
   unsigned long long *keys = new unsigned long long[n];
