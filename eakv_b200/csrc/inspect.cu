@@ -90,34 +90,49 @@ validate_kernel(const uint8_t *__restrict__ buf, PageGeom g, int seq_len,
   if ((threadIdx.x & 31) == 0 && best != ~0ull) atomicMin(keys + lkv, best);
 }
 
-// One warp per (head, position) row; lane l writes dims 4l..4l+3 of each
-// 128-dim slice: four consecutive dims are four consecutive bytes of one
-// group, all low or all high nibbles.
+// One warp per (head, position) row, kRows rows per trip with all their
+// loads issued first; lane l writes dims 4l..4l+3 of each 128-dim slice:
+// four consecutive dims are four consecutive bytes of one group, all low or
+// all high nibbles.
+constexpr int kRows = 4;
+
 __global__ void __launch_bounds__(kThreads)
 dequant_kernel(const uint8_t *__restrict__ buf, PageGeom g, int head_dim, int lkv, int pos_begin,
                int n_pos, float *__restrict__ out) {
   const int lane = threadIdx.x & 31;
   const long long rows = (long long)g.n_heads * n_pos;
   const long long warps = (long long)gridDim.x * (kThreads / 32);
-  for (long long row = (long long)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < rows;
-       row += warps) {
-    const int h = (int)(row / n_pos);
-    const int t = pos_begin + (int)(row - (long long)h * n_pos);
-    const int page = t / kPagePositions, pip = t - page * kPagePositions;
-    const uint8_t *pp = buf + (((size_t)lkv * g.n_heads + h) * g.n_pages + page) * g.page_bytes;
-    float *o = out + row * head_dim;
+  for (long long row0 = ((long long)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5)) * kRows;
+       row0 < rows; row0 += warps * kRows) {
     for (int d = 4 * lane; d < head_dim; d += 128) {
       const int grp = d >> 6, k = d & 63;
-      const int slot = pip * g.gpd + grp;
-      const uint32_t w = *reinterpret_cast<const uint32_t *>(pp + (size_t)slot * 32 + (k & 31));
-      const float2 sb = reinterpret_cast<const float2 *>(pp + g.nib_bytes)[slot];
       const int sh = k < 32 ? 0 : 4;
-      float4 v;
-      v.x = fmaf((float)((w >> sh) & 15), sb.x, sb.y);
-      v.y = fmaf((float)((w >> (8 + sh)) & 15), sb.x, sb.y);
-      v.z = fmaf((float)((w >> (16 + sh)) & 15), sb.x, sb.y);
-      v.w = fmaf((float)((w >> (24 + sh)) & 15), sb.x, sb.y);
-      *reinterpret_cast<float4 *>(o + d) = v;
+      uint32_t w[kRows];
+      float2 sb[kRows];
+#pragma unroll
+      for (int r = 0; r < kRows; r++) {
+        const long long row = row0 + r;
+        if (row < rows) {
+          const int h = (int)(row / n_pos);
+          const int t = pos_begin + (int)(row - (long long)h * n_pos);
+          const int page = t / kPagePositions, pip = t - page * kPagePositions;
+          const uint8_t *pp = buf + (((size_t)lkv * g.n_heads + h) * g.n_pages + page) * g.page_bytes;
+          const int slot = pip * g.gpd + grp;
+          w[r] = *reinterpret_cast<const uint32_t *>(pp + (size_t)slot * 32 + (k & 31));
+          sb[r] = reinterpret_cast<const float2 *>(pp + g.nib_bytes)[slot];
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kRows; r++) {
+        const long long row = row0 + r;
+        if (row >= rows) break;
+        float4 v;
+        v.x = fmaf((float)((w[r] >> sh) & 15), sb[r].x, sb[r].y);
+        v.y = fmaf((float)((w[r] >> (8 + sh)) & 15), sb[r].x, sb[r].y);
+        v.z = fmaf((float)((w[r] >> (16 + sh)) & 15), sb[r].x, sb[r].y);
+        v.w = fmaf((float)((w[r] >> (24 + sh)) & 15), sb[r].x, sb[r].y);
+        *reinterpret_cast<float4 *>(out + row * head_dim + d) = v;
+      }
     }
   }
 }
