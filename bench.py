@@ -594,7 +594,7 @@ def run_b200(args, cfg, world, rank, local):
 
 
 def run_ggml(args, world, rank, local):
-    """The q4_1_eakv ggml block type (SURVEY next row 1): from_float,
+    """The q4_1_eakv ggml block type (llama.cpp integration): from_float,
     to_float and vec_dot on device buffers, one JSON line each, with the
     reference's AVX-512 code (or its restatement) timed on one host thread
     on a bounded sample. HBM-bound; 1 GiB of f32 per pass (> L2)."""
@@ -703,7 +703,7 @@ def _time(fn, args, stream):
 
 
 def run_inspect(args, world, rank, local):
-    """Device validate and dequantize (SURVEY next rows 3, 4) on one cfg4
+    """Device validate and dequantize of a resident cache on one cfg4
     sequence (32 layers x 8 KV heads x 32768 positions, 1.34 GB of pages)."""
     import torch
     import eakv_b200 as E
@@ -733,7 +733,7 @@ def run_inspect(args, world, rank, local):
 
 
 def run_llama(args, world, rank, local):
-    """llama.cpp state import (SURVEY next row 2): host state buffer in,
+    """llama.cpp state import: host state buffer in,
     device cache out, PCIe inside the timed region (the API's own
     contract); the reference bridge on the host cores beside it."""
     import ctypes
