@@ -11,10 +11,13 @@ sequence over every layer (softmax(QK^T/sqrt d)V on the Q4 cache).
 
 Default workload (N=1): config 4 of BASELINE.json, the shape the north-star
 target is quoted on - Llama-3-8B GQA 4:1, 32 layers, 32 Q / 8 KV heads,
-head_dim 128, 32768 cached positions, 16 independent sequences per GPU
-(21.5 GB of Q4 cache per GPU, far above the 126 MB L2, so no flush is
-needed). Under torchrun every rank holds its own 16 sequences (weak scaling,
-no data-path collective); rank 0 prints one JSON line with the whole-job
+head_dim 128, 32768 cached positions, 16 sequences (21.5 GB of Q4 cache,
+far above the 126 MB L2, so no flush is needed). Under torchrun (N > 1) the
+same 16 sequences are spread over the N GPUs (strong scaling): N/2 KV-head
+shards, each split in two by sequence, so every step's NCCL all-gather of
+the (output, LSE) records and their merge are inside the timed region;
+--dp instead gives every rank its own 16 sequences (weak scaling, no
+data-path collective). Rank 0 prints one JSON line with the whole-job
 throughput and the max-over-ranks step time.
 
 --impl reference times the reference's CPU implementation of the same step
@@ -48,8 +51,9 @@ CONFIGS = {
     # (restore to S-1, append, advance) and then attends all S positions
     3: dict(workload="cfg3 Llama-2-7B MHA d128 S8192 B1 + 1-token append per step", L=32,
             nq=32, nkv=32, hd=128, S=8192, B=1, append=True),
+    # multi-GPU: KV-head shards x a two-way sequence split (strong scaling)
     4: dict(workload="cfg4 Llama-3-8B GQA 4:1 d128 S32768 B16", L=32, nq=32, nkv=8, hd=128,
-            S=32768, B=16),
+            S=32768, B=16, shard=True, seq_shards=2),
     # multi-GPU: the KV heads (with their query heads) are sharded over the
     # GPUs; beyond one KV head per GPU (or with --seq-shards) every rank of a
     # head shard holds a page-aligned slice of every sequence, and the
@@ -257,7 +261,8 @@ def run_reference(args, cfg, world, rank):
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": cfg["B"] * cfg["S"] / value * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong" if cfg.get("shard") else "weak",
+        "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,1) K/V, per-channel log-uniform[0.5,8] K scale)",
         "config": config_json(cfg, world), "impl": "reference",
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
@@ -268,24 +273,31 @@ def run_reference(args, cfg, world, rank):
 
 
 def layout(cfg, world, seq_shards=0):
-    """(head shards, sequence shards) of a sharded config on `world` ranks."""
+    """(head shards, sequence shards) of a sharded config on `world` ranks;
+    seq_shards 0 takes the config's own choice."""
     if not cfg.get("shard") or world == 1:
         return 1, 1
     from eakv_b200.parallel import shard_layout
-    return shard_layout(world, cfg["nkv"], seq_shards)
+    ss = seq_shards or cfg.get("seq_shards", 0)
+    if ss and world % ss:
+        ss = 0
+    return shard_layout(world, cfg["nkv"], ss)
 
 
 def config_json(cfg, world, seq_shards=0):
     hs, ss = layout(cfg, world, seq_shards)
     sharded = bool(cfg.get("shard"))
-    if sharded:
+    if sharded and world > 1:
         par = (f"kv-head shards x{hs}, sequence split x{ss}"
-               + (" (NCCL all-gather + LSE merge)" if ss > 1 else " (no data-path collective)"))
+               + (" (NCCL all-gather of (output, LSE) records + exact merge, in the library)"
+                  if ss > 1 else " (no data-path collective)"))
+    elif sharded:
+        par = "single GPU"
     else:
         par = f"dp{world} (independent sequences per GPU)"
     return {"workload": cfg["workload"], "layers": cfg["L"], "q_heads": cfg["nq"],
             "kv_heads": cfg["nkv"], "head_dim": cfg["hd"], "seq_len": cfg["S"],
-            "batch_per_gpu": cfg["B"], "global_batch": cfg["B"] * (1 if sharded else world),
+            "sequences": cfg["B"], "global_batch": cfg["B"] * (1 if sharded else world),
             "parallelism": par,
             "bytes_per_kv_token": bytes_per_token(cfg),
             "l2": ("L2 flushed before every timed step (512 MB device write, outside the "
@@ -351,8 +363,9 @@ def run_b200(args, cfg, world, rank, local):
     sub = None
     if split:
         import torch.distributed as dist
-        from eakv_b200.parallel import SeqSplitDecoder, seq_shard
-        # one process group per head shard (every rank creates every group)
+        from eakv_b200.parallel import seq_shard
+        # one process group per head shard (every rank creates every group);
+        # it only carries the NCCL id of the library's communicator
         for h in range(hs):
             g_ = dist.new_group(ranks=[h * ss + k for k in range(ss)])
             if h == rank // ss:
@@ -368,12 +381,17 @@ def run_b200(args, cfg, world, rank, local):
     stream = torch.cuda.Stream(dev)
     torch.cuda.set_stream(stream)
     sh = stream.cuda_stream
-    qs = [torch.randn(B, L, nq, hd, device=dev) for _ in range(4)]
+    # the ranks of one head shard attend with the same queries
+    gq = torch.Generator(device=dev)
+    gq.manual_seed(4321 + rank // ss)
+    qs = [torch.randn(B, L, nq, hd, device=dev, generator=gq) for _ in range(4)]
     out = torch.empty(B, L, nq, hd, device=dev)
     launches_per_step = E.decode_launches(caches, nq)
+    decoder = None
     if split:
-        decoder = SeqSplitDecoder(caches, nq, hd, group=sub)
-        launches_per_step += 1   # the merge kernel
+        from eakv_b200.parallel import SeqSplitDecoder
+        decoder = SeqSplitDecoder(caches, nq, hd, group=sub, device=local)
+        launches_per_step += 1   # the merge kernel after the all-gather
 
     appending = bool(cfg.get("append"))
     if appending:
@@ -392,7 +410,7 @@ def run_b200(args, cfg, world, rank, local):
             if mid is not None:
                 mid.record(stream)   # decode launch time = this event -> step end
         if split:
-            decoder.step(q_in.view(B * L * nq, hd), o.view(B * L * nq, hd), stream=stream)
+            decoder.step(q_in, o, stream=sh)
         else:
             E.decode_attention(caches, q_in, nq, o, stream=sh)
 
@@ -568,9 +586,9 @@ def run_b200(args, cfg, world, rank, local):
             "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded torch.randn K/V on device, per-channel log-uniform[0.5,8] "
                     "K scale, 4-slice pool rotated over caches/layers)",
-            "config": dict(config_json(cfg, world, args.seq_shards),
-                           step_launch=("CUDA graph replay of the library calls" if use_graph
-                                        else "direct library calls")),
+            "config": config_json(cfg, world, args.seq_shards),
+            "step_launch": ("CUDA graph replay of the library calls" if use_graph
+                            else "direct library calls"),
             "e2e": {"value": tokens_step / (e2e_ms / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": int(qh.nbytes) + (int(kv_host.numel()) * 4
                                                             if appending else 0),
@@ -588,6 +606,10 @@ def run_b200(args, cfg, world, rank, local):
             "device_status": status,
         }
         print(json.dumps(result), flush=True)
+    if decoder is not None:
+        torch.cuda.synchronize()
+        barrier()
+        decoder.close()
     for c in caches:
         c.free()
     return result
@@ -702,6 +724,153 @@ def _time(fn, args, stream):
     return e0.elapsed_time(e1) / args.steps
 
 
+TWOCALL_SHAPES = [
+    # the reference benchmark's shapes (benchmarks/bench_libeakv.c:160-164: MHA,
+    # 8 heads, head_dim 128), then one layer of a cfg4 sequence (GQA 4:1)
+    ("reference bench 7B-like 1L 8H d128 S2048", 1, 8, 8, 128, 2048),
+    ("reference bench 7B-like 1L 8H d128 S8192", 1, 8, 8, 128, 8192),
+    ("reference bench 7B-like 32L 8H d128 S2048", 32, 8, 8, 128, 2048),
+    ("cfg4 one layer of one sequence: 32 Q / 8 KV heads d128 S32768", 1, 32, 8, 128, 32768),
+]
+
+
+def run_twocall(args, world, rank, local):
+    """The reference's own API calls on the device cache, each on the
+    shapes the reference benchmark times (benchmarks/bench_libeakv.c:131-151,
+    :186-191, :222-223) and on one cfg4 layer: the two-call attention
+    (eakv_attention_scores / eakv_attention_output) on device buffers, timed
+    with CUDA events after an L2 flush, with their HBM roofline; the same
+    calls with host buffers (the reference's contract, PCIe and the host
+    synchronization included, wall clock); load_raw from host f32; save and
+    load of the .eakv file. The reference's host code with the restated
+    kernels (oracle/_ref) runs the same calls on one host thread beside it.
+    Weights for the V sum are the softmax of the scores."""
+    import ctypes
+    import tempfile
+    import torch
+    import eakv_b200 as E
+    from oracle import oracle as O
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    E.set_device(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    peak, peak_kind = measured_peak()
+    R = O.rlib() if O.ref_available() else None
+    rng = np.random.default_rng(0)
+
+    def line(metric, value, unit, ms, workload, nbytes=None, cpu=None, launches=None):
+        roof = None
+        if nbytes is not None:
+            gbs = nbytes / (ms / 1e3) / 1e9
+            roof = {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                    "frac": gbs / peak, "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
+                    "algorithmic_bytes_per_launch": nbytes}
+        print(json.dumps({
+            "metric": metric, "value": value, "unit": unit, "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+            "config": {"workload": workload, "l2": "L2 flushed before every timed call"},
+            "roofline": roof, "cpu_baseline": cpu, "gpu_launches": launches}), flush=True)
+
+    def dev_time(fn):
+        for _ in range(args.warmup):
+            fn()
+        ts = []
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            ts.append((e0, e1))
+        torch.cuda.synchronize()
+        return sorted(a.elapsed_time(b) for a, b in ts)[len(ts) // 2]
+
+    def wall(fn, reps):
+        fn()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        return (time.perf_counter() - t0) / reps * 1e3
+
+    for name, L, nq, nkv, hd, S in TWOCALL_SHAPES:
+        data = rng.standard_normal((L, 2, nkv, S, hd), dtype=np.float32)
+        c = E.Cache(L, nkv, hd, S)
+        c.set_stream(stream.cuda_stream)
+        ms_load = wall(lambda: c.load_raw(data, S), max(2, min(args.steps, 5)))
+        q = rng.standard_normal(nq * hd, dtype=np.float32)
+        dq = torch.from_numpy(q).to(dev)
+        dsc = torch.empty(nq * S, device=dev)
+        dout = torch.empty(nq * hd, device=dev)
+        q4 = nkv * S * (hd // 64) * 40                     # Q4 bytes of one (layer, K/V)
+        ms_s = dev_time(lambda: c.scores_device(dq, 0, nq, nkv, dsc))
+        w = torch.softmax(dsc.view(nq, S), dim=1).reshape(-1).contiguous()
+        ms_o = dev_time(lambda: c.output_device(w, 0, nq, nkv, dout))
+        torch.cuda.synchronize()
+        wh = w.cpu().numpy()
+        ms_sh = wall(lambda: c.scores(q, 0, nq, nkv), max(3, args.steps))
+        ms_oh = wall(lambda: c.output(wh, 0, nq, nkv), max(3, args.steps))
+        with tempfile.TemporaryDirectory() as td:
+            path = os.path.join(td, "c.eakv")
+            ms_save = wall(lambda: c.save(path), 3)
+            fsize = os.path.getsize(path)
+            ms_fload = wall(lambda: E.Cache.load(path).free(), 3)
+            cpu = {}
+            if R is not None:
+                rc_ = R.eakv_cache_create(L, nkv, hd, S)
+                sc = np.zeros(nq * S, np.float32)
+                out = np.zeros(nq * hd, np.float32)
+                reps = max(1, min(20, int(2e8 // (nq * S * hd))))
+                cpu["load_raw"] = wall(lambda: R.eakv_cache_load_raw(rc_, data.ctypes.data, S), 2)
+                cpu["scores"] = wall(lambda: R.eakv_attention_scores(
+                    rc_, q.ctypes.data, 0, nq, nkv, sc.ctypes.data), reps)
+                cpu["output"] = wall(lambda: R.eakv_attention_output(
+                    rc_, wh.ctypes.data, 0, nq, nkv, out.ctypes.data), reps)
+                rpath = os.path.join(td, "r.eakv").encode()
+                cpu["save"] = wall(lambda: R.eakv_cache_save(rc_, rpath), 2)
+
+                def rload():
+                    h = ctypes.c_void_p()
+                    R.eakv_cache_load(rpath, ctypes.byref(h))
+                    R.eakv_cache_free(h)
+                cpu["load"] = wall(rload, 2)
+                R.eakv_cache_free(rc_)
+
+        def cb(op, value, unit):
+            if op not in cpu:
+                return None
+            return {"value": value(cpu[op]), "unit": unit, "cores": 1, "kind": "reference",
+                    "sample": f"the same call on the reference's host code, {op}"}
+
+        sc_bytes = q4 + nq * S * 4 + nq * hd * 4
+        out_bytes = q4 + nq * S * 4 + nq * hd * 4
+        wl = f"{name} ({L} layer(s) cached, layer 0 attended)"
+        line("attention_scores device: KV positions/s", nkv * S / (ms_s / 1e3), "KV head-positions/s",
+             ms_s, wl, nbytes=sc_bytes, launches=1,
+             cpu=cb("scores", lambda t: nkv * S / (t / 1e3), "KV head-positions/s"))
+        line("attention_output device: KV positions/s", nkv * S / (ms_o / 1e3), "KV head-positions/s",
+             ms_o, wl, nbytes=out_bytes, launches=None,
+             cpu=cb("output", lambda t: nkv * S / (t / 1e3), "KV head-positions/s"))
+        line("attention_scores host API (copies + sync, wall clock): KV positions/s",
+             nkv * S / (ms_sh / 1e3), "KV head-positions/s", ms_sh, wl,
+             cpu=cb("scores", lambda t: nkv * S / (t / 1e3), "KV head-positions/s"))
+        line("attention_output host API (copies + sync, wall clock): KV positions/s",
+             nkv * S / (ms_oh / 1e3), "KV head-positions/s", ms_oh, wl,
+             cpu=cb("output", lambda t: nkv * S / (t / 1e3), "KV head-positions/s"))
+        line("load_raw from host f32 (PCIe + quantize, wall clock) GB/s of f32", data.nbytes /
+             (ms_load / 1e3) / 1e9, "GB/s", ms_load, wl,
+             cpu=cb("load_raw", lambda t: data.nbytes / (t / 1e3) / 1e9, "GB/s"))
+        line("save .eakv GB/s of file (wall clock)", fsize / (ms_save / 1e3) / 1e9, "GB/s",
+             ms_save, wl, cpu=cb("save", lambda t: fsize / (t / 1e3) / 1e9, "GB/s"))
+        line("load .eakv GB/s of file (wall clock)", fsize / (ms_fload / 1e3) / 1e9, "GB/s",
+             ms_fload, wl, cpu=cb("load", lambda t: fsize / (t / 1e3) / 1e9, "GB/s"))
+        c.free()
+
+
 def run_inspect(args, world, rank, local):
     """Device validate and dequantize of a resident cache on one cfg4
     sequence (32 layers x 8 KV heads x 32768 positions, 1.34 GB of pages)."""
@@ -785,9 +954,11 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", type=int, default=4, choices=sorted(CONFIGS))
-    ap.add_argument("--op", default="decode", choices=["decode", "ggml", "inspect", "llama"],
-                    help="time another part instead: the q4_1_eakv ggml type kernels, device "
-                         "validate + dequantize, or the llama.cpp state import")
+    ap.add_argument("--op", default="decode",
+                    choices=["decode", "twocall", "ggml", "inspect", "llama"],
+                    help="time another part instead: the reference's two-call attention API "
+                         "and its load_raw / save / load, the q4_1_eakv ggml type kernels, "
+                         "device validate + dequantize, or the llama.cpp state import")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
@@ -797,8 +968,12 @@ def main():
     ap.add_argument("--force-simt", action="store_true",
                     help="time the CUDA-core decode kernel even where tensor cores apply")
     ap.add_argument("--seq-shards", type=int, default=0,
-                    help="sharded configs: ranks per sequence split (0: as many KV-head "
-                         "shards as divide the ranks, the rest split the sequence)")
+                    help="sharded configs: ranks per sequence split (0: the config's "
+                         "choice - cfg4 two, cfg5 as many KV-head shards as divide the "
+                         "ranks and the rest split the sequence)")
+    ap.add_argument("--dp", action="store_true",
+                    help="cfg4 under torchrun: every rank decodes its own 16 sequences "
+                         "(weak scaling, no data-path collective) instead of sharding them")
     ap.add_argument("--graph", default="auto", choices=["auto", "on", "off"],
                     help="replay the device step from CUDA graphs (auto: for the small, "
                          "launch-latency-bound configs that flush L2 between steps)")
@@ -808,6 +983,8 @@ def main():
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     cfg = dict(CONFIGS[args.config])
+    if args.dp:
+        cfg["shard"] = False
     if args.batch:
         cfg["B"] = args.batch
         cfg["workload"] += f" (batch overridden to {args.batch})"
@@ -816,7 +993,9 @@ def main():
         cfg["workload"] += f" (seq_len overridden to {args.seq})"
     world, rank, local = dist_setup(args.gpus)
     try:
-        if args.op == "ggml":
+        if args.op == "twocall":
+            run_twocall(args, world, rank, local)
+        elif args.op == "ggml":
             run_ggml(args, world, rank, local)
         elif args.op == "inspect":
             run_inspect(args, world, rank, local)

@@ -75,15 +75,24 @@ SIGNATURES = {
     "eakv_decode_attention_host": (_I, [_P, _I, _P, _I, _P, _P]),
     "eakv_decode_attention_noalloc": (_I, [_P, _I, _P, _I, _P, _P]),
     "eakv_decode_launches": (_I, [_P, _I, _I]),
+    "eakv_decode_splits": (_I, [_P, _I, _I]),
     "eakv_decode_attention_partial": (_I, [_P, _I, _P, _I, _I, _I, _P, _P, _P]),
     "eakv_lse_combine": (_I, [_I, _I, _I, _P, _P, _P, _P, _P]),
     "eakv_test_force_splits": (_I, [_I]),
     "eakv_test_force_path": (_I, [_I]),
     "eakv_test_choose_splits": (_I, [_c.c_longlong, _I, _I, _I, _I, _I]),
     "eakv_test_stall": (_I, [_I, ctypes.c_uint]),
+    "eakv_test_separate_merge": (_I, [_I]),
     "eakv_cache_validate": (_I, [_P, _P]),
     "eakv_cache_dequantize_device": (_I, [_P, _I, _I, _I, _I, _P, _P]),
     "eakv_cache_dequantize": (_I, [_P, _I, _I, _I, _I, _P]),
+    # eakv_nccl.h
+    "eakv_nccl_version": (_I, []),
+    "eakv_nccl_unique_id": (_I, [_P]),
+    "eakv_nccl_comm_init": (_I, [_c.POINTER(_P), _I, _P, _I, _I]),
+    "eakv_nccl_comm_destroy": (_I, [_P]),
+    "eakv_nccl_comm_abort": (_I, [_P]),
+    "eakv_decode_attention_split": (_I, [_P, _I, _P, _I, _I, _I, _P, _P, _P]),
     # eakv_ggml.h
     "eakv_quantize_row": (None, [_P, _P, _c.c_int64]),
     "eakv_dequantize_row": (None, [_P, _P, _c.c_int64]),
@@ -303,6 +312,18 @@ class Cache:
         return out
 
     # --- device entry points ------------------------------------------------------
+    def scores_device(self, d_queries, layer, n_q, n_kv, d_scores):
+        """eakv_attention_scores_device: f32[n_q][seq_len] scores on the device."""
+        return _check(lib().eakv_attention_scores_device(self.h, _ptr(d_queries), layer, n_q, n_kv,
+                                                         _ptr(d_scores)),
+                      "eakv_attention_scores_device")
+
+    def output_device(self, d_weights, layer, n_q, n_kv, d_output):
+        """eakv_attention_output_device: f32[n_q][head_dim] outputs on the device."""
+        return _check(lib().eakv_attention_output_device(self.h, _ptr(d_weights), layer, n_q, n_kv,
+                                                         _ptr(d_output)),
+                      "eakv_attention_output_device")
+
     def load_raw_device(self, d_data, seq_len):
         return lib().eakv_cache_load_raw_device(self.h, _ptr(d_data), seq_len)
 
@@ -363,8 +384,66 @@ def lse_combine(n_parts, n_rows, head_dim, d_parts, d_lse, d_output, d_lse_out=N
                   "eakv_lse_combine")
 
 
+# --- sequence split over NCCL (include/eakv_nccl.h) -------------------------------
+NCCL_ID_BYTES = 128
+
+
+def nccl_version():
+    """NCCL version code of the library's NCCL (< 0: unavailable)."""
+    return lib().eakv_nccl_version()
+
+
+def nccl_unique_id():
+    """A new NCCL unique id (bytes) for eakv_nccl_comm_init."""
+    buf = ctypes.create_string_buffer(NCCL_ID_BYTES)
+    _check(lib().eakv_nccl_unique_id(buf), "eakv_nccl_unique_id")
+    return buf.raw
+
+
+class NcclComm:
+    """A communicator of the library's NCCL (eakv_nccl_comm_init): n_ranks
+    ranks, this one `rank`, on CUDA device `device`; blocks until every rank
+    has joined."""
+
+    def __init__(self, n_ranks, unique_id, rank, device):
+        if len(unique_id) != NCCL_ID_BYTES:
+            raise ValueError("bad NCCL unique id")
+        h = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(bytes(unique_id), NCCL_ID_BYTES)
+        _check(lib().eakv_nccl_comm_init(ctypes.byref(h), n_ranks, buf, rank, device),
+               "eakv_nccl_comm_init")
+        self.h = h.value
+        self.n_ranks, self.rank, self.device = n_ranks, rank, device
+
+    def destroy(self):
+        if self.h:
+            _check(lib().eakv_nccl_comm_destroy(self.h), "eakv_nccl_comm_destroy")
+            self.h = None
+
+    def abort(self):
+        if self.h:
+            lib().eakv_nccl_comm_abort(self.h)
+            self.h = None
+
+
+def decode_attention_split(caches, d_queries, n_q_heads, d_output, comm, pos_begin=0,
+                           pos_end=-1, stream=None):
+    """eakv_decode_attention_split: this rank's slice of every sequence,
+    merged with the other ranks' over `comm` (an NcclComm)."""
+    arr = _handles(caches)
+    return _check(lib().eakv_decode_attention_split(arr, len(caches), _ptr(d_queries), n_q_heads,
+                                                    pos_begin, pos_end, _ptr(d_output), comm.h,
+                                                    stream),
+                  "eakv_decode_attention_split")
+
+
 def decode_launches(caches, n_q_heads):
     return lib().eakv_decode_launches(_handles(caches), len(caches), n_q_heads)
+
+
+def decode_splits(caches, n_q_heads):
+    """Sequence splits per row the planner picks for these caches."""
+    return lib().eakv_decode_splits(_handles(caches), len(caches), n_q_heads)
 
 
 def set_device(device):
@@ -386,6 +465,12 @@ def choose_splits(items, max_pages, lo, hi, per_sm, sms):
     (host code only: runs without a GPU)."""
     return lib().eakv_test_choose_splits(int(items), int(max_pages), int(lo), int(hi),
                                          int(per_sm), int(sms))
+
+
+def separate_merge(on):
+    """Test aid: merge sequence splits in a second kernel (True) instead of
+    inside the decode kernel (False, the default)."""
+    lib().eakv_test_separate_merge(1 if on else 0)
 
 
 def force_path(path):

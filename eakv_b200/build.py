@@ -6,7 +6,8 @@
 Each csrc/*.cu is compiled by nvcc for sm_100a only (-gencode
 arch=compute_100a,code=sm_100a) into _build/, then linked into
 eakv_b200/libeakv_b200.so with the CUDA runtime linked statically, so the
-library carries no dependency on a particular libcudart.so. The kernels
+library carries no dependency on a particular libcudart.so; NCCL is
+resolved at run time (split.cu), so it is no link dependency either. The kernels
 whose results must equal the reference bit for bit (quantize, the two-call
 attention API, file I/O) are compiled with -fmad=false on top of the
 explicit round-to-nearest intrinsics they already use.
@@ -74,7 +75,7 @@ def build(force=False, verbose=False, extra=()):
     objs = [o for o, _ in results]
     if (force or not os.path.exists(LIB)
             or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs)):
-        cmd = [nvcc()] + ARCH + ["-shared", "-cudart", "static", "-o", LIB] + objs
+        cmd = [nvcc()] + ARCH + ["-shared", "-cudart", "static", "-o", LIB] + objs + ["-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("link failed:\n" + " ".join(cmd) + "\n" + r.stdout + r.stderr)

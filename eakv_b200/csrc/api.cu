@@ -21,6 +21,8 @@ thread_local int t_force_path = 0;
 // Stalled page and wait budget set by eakv_test_stall() on this host thread.
 thread_local int t_test_stall = 0;
 thread_local unsigned t_wait_budget = 0;
+// Separate merge kernel selected by eakv_test_separate_merge() on this thread.
+thread_local int t_sep_merge = 0;
 
 int *device_status_ptr() {
   static std::atomic<int *> ptrs[64];
@@ -39,12 +41,6 @@ int *device_status_ptr() {
   }
   return p;
 }
-
-}  // namespace eakv
-
-using namespace eakv;
-
-namespace {
 
 int check_batch(const eakv_cache_t *const *caches, int n, int n_q, const char *who) {
   if (!caches || n <= 0 || n > kMaxBatch) {
@@ -77,6 +73,7 @@ int check_batch(const eakv_cache_t *const *caches, int n, int n_q, const char *w
   return EAKV_OK;
 }
 
+// Call after the device guard: the status word is the current device's.
 DecodeArgs base_args(const eakv_cache_t *c0, int n_caches, int n_q) {
   DecodeArgs a;
   memset(&a, 0, sizeof a);
@@ -93,6 +90,7 @@ DecodeArgs base_args(const eakv_cache_t *c0, int n_caches, int n_q) {
   a.force_path = t_force_path;
   a.test_stall = t_test_stall;
   a.wait_budget = t_wait_budget;
+  a.sep_merge = t_sep_merge;
   return a;
 }
 
@@ -103,18 +101,39 @@ void fill_batch(DecodeBatch &b, const eakv_cache_t *const *caches, int n) {
   }
 }
 
-// Runs the decode with workspace from the first cache's scratch, placed
-// after `reserve` bytes the caller already uses there.
-int run_decode(const eakv_cache_t *c0, DecodeArgs &a, const DecodeBatch &b, size_t reserve,
-               cudaStream_t s) {
-  size_t ws = decode_workspace_bytes(a, b);
-  void *w = nullptr;
-  if (ws) {
-    uint8_t *base = (uint8_t *)cache_scratch(c0, reserve + ws);
-    if (!base) return EAKV_ERR_ALLOC;
-    w = base + reserve;
+}  // namespace eakv
+
+using namespace eakv;
+
+namespace {
+
+// Status word of the current device into a.status; EAKV_ERR_INVALID when its
+// address cannot be looked up (the kernels would have nowhere to report).
+int attach_status(DecodeArgs &a, const char *who) {
+  if (!a.status) {
+    set_error(EAKV_ERR_INVALID, "%s: device status word unavailable", who);
+    return EAKV_ERR_INVALID;
   }
-  return decode_launch(a, b, w, ws, s);
+  return EAKV_OK;
+}
+
+// Runs the decode with its split counters and workspace from the first
+// cache's scratch, the workspace placed after `reserve` bytes the caller
+// already uses there.
+int run_decode(const eakv_cache_t *c0, DecodeArgs &a, const DecodeBatch &b, size_t reserve,
+               cudaStream_t s, const char *who) {
+  int rc = attach_status(a, who);
+  if (rc) return rc;
+  const size_t ws = decode_workspace_bytes(a, b);
+  const size_t nc = decode_counters(a, b);
+  void *w = nullptr;
+  if (ws || nc) {
+    void *base = nullptr;
+    rc = cache_workspace(c0, nc, reserve + ws, &a.cnt, &base);
+    if (rc) return rc;
+    w = (uint8_t *)base + reserve;
+  }
+  return decode_launch(a, b, ws ? w : nullptr, ws, s);
 }
 
 // ---- pipelined host-buffer decode -------------------------------------------
@@ -197,7 +216,13 @@ int decode_host_pipelined(const eakv_cache_t *const *caches, DecodeArgs a, const
   HostStreams hs;
   int rc = host_streams(c0->device, hs);
   if (rc) return rc;
+  rc = attach_status(a, "decode_attention_host");
+  if (rc) return rc;
   decode_fix_plan(a, b);
+  // split counters: one per work item of the whole batch; a chunk's items
+  // are a contiguous run of them (items are ordered cache, layer, head, ...)
+  const size_t n_cnt = decode_counters(a, b);
+  const size_t items_per_unit = n_cnt / units;
 
   DecodeArgs ca[4];
   DecodeBatch cb[4];
@@ -218,8 +243,12 @@ int decode_host_pipelined(const eakv_cache_t *const *caches, DecodeArgs a, const
   }
   ws = (ws + 255) / 256 * 256;
   // [queries | outputs | workspace of stream s | workspace of the second stream]
-  uint8_t *base = (uint8_t *)cache_scratch(c0, 2 * half + 2 * ws);
-  if (!base) return EAKV_ERR_ALLOC;
+  void *vbase = nullptr;
+  unsigned *cnt0 = nullptr;
+  rc = cache_workspace(c0, n_cnt, 2 * half + 2 * ws, &cnt0, &vbase);
+  if (rc) return rc;
+  uint8_t *base = (uint8_t *)vbase;
+  for (int k = 0; k < nch; k++) ca[k].cnt = n_cnt ? cnt0 + start[k] * items_per_unit : nullptr;
   float *dq = (float *)base, *dout = (float *)(base + half);
 
   cudaEvent_t ev[9] = {};
@@ -316,7 +345,7 @@ int eakv_attention_fused_device(const eakv_cache_t *c, const float *d_q, int lay
   a.out = d_out;
   DecodeBatch b;
   fill_batch(b, cs, 1);
-  return run_decode(c, a, b, 0, c->stream);
+  return run_decode(c, a, b, 0, c->stream, "attention_fused");
 }
 
 int eakv_attention_fused(const eakv_cache_t *c, const float *queries, int layer, int n_q,
@@ -337,9 +366,13 @@ int eakv_attention_fused(const eakv_cache_t *c, const float *queries, int layer,
   a.n_layers = 1;
   DecodeBatch b;
   fill_batch(b, cs, 1);
+  rc = attach_status(a, "attention_fused");
+  if (rc) return rc;
   size_t ws = decode_workspace_bytes(a, b);
-  uint8_t *base = (uint8_t *)cache_scratch(c, reserve + ws);
-  if (!base) return EAKV_ERR_ALLOC;
+  void *vbase = nullptr;
+  rc = cache_workspace(c, decode_counters(a, b), reserve + ws, &a.cnt, &vbase);
+  if (rc) return rc;
+  uint8_t *base = (uint8_t *)vbase;
   float *d_q = (float *)base;
   float *d_o = (float *)(base + reserve / 2);
   a.q = d_q;
@@ -372,18 +405,27 @@ int eakv_decode_attention(const eakv_cache_t *const *caches, int n_caches, const
   a.out = d_out;
   DecodeBatch b;
   fill_batch(b, caches, n_caches);
-  return run_decode(c0, a, b, 0, s);
+  return run_decode(c0, a, b, 0, s, "decode_attention");
 }
 
 int eakv_decode_launches(const eakv_cache_t *const *caches, int n_caches, int n_q) {
   clear_error();
   int rc = check_batch(caches, n_caches, n_q, "decode_launches");
   if (rc) return rc;
+  // the split merge runs inside the decode kernel
+  return 1;
+}
+
+int eakv_decode_splits(const eakv_cache_t *const *caches, int n_caches, int n_q) {
+  clear_error();
+  int rc = check_batch(caches, n_caches, n_q, "decode_splits");
+  if (rc) return rc;
   DeviceGuard g(caches[0]->device);
   DecodeArgs a = base_args(caches[0], n_caches, n_q);
   DecodeBatch b;
   fill_batch(b, caches, n_caches);
-  return decode_workspace_bytes(a, b) ? 2 : 1;
+  decode_fix_plan(a, b);
+  return a.fix_n_splits;
 }
 
 int eakv_decode_attention_host(const eakv_cache_t *const *caches, int n_caches,
@@ -409,9 +451,13 @@ int eakv_decode_attention_host(const eakv_cache_t *const *caches, int n_caches,
   const int nch = n * sizeof(float) >= kPipelineMinBytes ? host_chunks(units, start) : 1;
   if (nch > 1) return decode_host_pipelined(caches, a, b, queries, output, s, units, start, nch);
 
+  rc = attach_status(a, "decode_attention_host");
+  if (rc) return rc;
   size_t ws = decode_workspace_bytes(a, b);
-  uint8_t *base = (uint8_t *)cache_scratch(c0, 2 * half + ws);
-  if (!base) return EAKV_ERR_ALLOC;
+  void *vbase = nullptr;
+  rc = cache_workspace(c0, decode_counters(a, b), 2 * half + ws, &a.cnt, &vbase);
+  if (rc) return rc;
+  uint8_t *base = (uint8_t *)vbase;
   a.q = (float *)base;
   a.out = (float *)(base + half);
   rc = check_cuda(cudaMemcpyAsync((void *)a.q, queries, n * sizeof(float),
@@ -446,7 +492,7 @@ int eakv_decode_attention_partial(const eakv_cache_t *const *caches, int n_cache
   a.pos_end = pos_end;
   DecodeBatch b;
   fill_batch(b, caches, n_caches);
-  return run_decode(c0, a, b, 0, s);
+  return run_decode(c0, a, b, 0, s, "decode_attention_partial");
 }
 
 int eakv_lse_combine(int n_parts, int n_rows, int head_dim, const float *d_parts,
@@ -457,8 +503,8 @@ int eakv_lse_combine(int n_parts, int n_rows, int head_dim, const float *d_parts
     set_error(EAKV_ERR_INVALID, "lse_combine: invalid argument");
     return EAKV_ERR_INVALID;
   }
-  return lse_combine_launch(n_parts, n_rows, head_dim, d_parts, d_lse, d_out, d_lse_out,
-                            (cudaStream_t)stream);
+  return lse_combine_launch(n_parts, n_rows, head_dim, d_parts, (size_t)n_rows * head_dim, d_lse,
+                            (size_t)n_rows, d_out, d_lse_out, (cudaStream_t)stream);
 }
 
 }  // extern "C"
@@ -481,5 +527,10 @@ extern "C" int eakv_test_force_splits(int n) {
 extern "C" int eakv_test_stall(int page, unsigned wait_budget) {
   eakv::t_test_stall = page >= 0 ? page + 1 : 0;
   eakv::t_wait_budget = wait_budget;
+  return EAKV_OK;
+}
+
+extern "C" int eakv_test_separate_merge(int on) {
+  eakv::t_sep_merge = on ? 1 : 0;
   return EAKV_OK;
 }

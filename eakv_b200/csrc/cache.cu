@@ -39,21 +39,44 @@ int check_cuda(cudaError_t e, const char *what) {
   return code;
 }
 
+int cache_workspace(const eakv_cache *c, size_t n_counters, size_t bytes, unsigned **counters,
+                    void **data) {
+  const size_t have_data = c->d_scratch ? c->scratch_bytes - c->cnt_bytes : 0;
+  size_t cb = (n_counters * sizeof(unsigned) + 255) / 256 * 256;
+  if (!c->d_scratch || cb > c->cnt_bytes || bytes > have_data) {
+    // grow: neither region ever shrinks
+    if (cb < c->cnt_bytes) cb = c->cnt_bytes;
+    if (cb < 4096) cb = 4096;
+    size_t db = bytes > have_data ? bytes : have_data;
+    if (db < (1u << 20)) db = 1u << 20;
+    if (c->d_scratch) {
+      cudaStreamSynchronize(c->stream);
+      cudaFree(c->d_scratch);
+      c->d_scratch = nullptr;
+      c->scratch_bytes = c->cnt_bytes = 0;
+    }
+    void *p = nullptr;
+    int rc = check_cuda(cudaMalloc(&p, cb + db), "scratch allocation");
+    if (rc) return rc;
+    // the counters start at zero; the decode kernels leave them at zero
+    rc = check_cuda(cudaMemsetAsync(p, 0, cb, c->stream), "scratch counters");
+    if (!rc) rc = check_cuda(cudaStreamSynchronize(c->stream), "scratch counters");
+    if (rc) {
+      cudaFree(p);
+      return rc;
+    }
+    c->d_scratch = p;
+    c->cnt_bytes = cb;
+    c->scratch_bytes = cb + db;
+  }
+  if (counters) *counters = (unsigned *)c->d_scratch;
+  *data = (uint8_t *)c->d_scratch + c->cnt_bytes;
+  return EAKV_OK;
+}
+
 void *cache_scratch(const eakv_cache *c, size_t bytes) {
-  if (bytes <= c->scratch_bytes && c->d_scratch) return c->d_scratch;
-  if (c->d_scratch) {
-    cudaStreamSynchronize(c->stream);
-    cudaFree(c->d_scratch);
-    c->d_scratch = nullptr;
-    c->scratch_bytes = 0;
-  }
-  size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
-  if (check_cuda(cudaMalloc(&c->d_scratch, want), "scratch allocation") != EAKV_OK) {
-    c->d_scratch = nullptr;
-    return nullptr;
-  }
-  c->scratch_bytes = want;
-  return c->d_scratch;
+  void *d = nullptr;
+  return cache_workspace(c, 0, bytes, nullptr, &d) == EAKV_OK ? d : nullptr;
 }
 
 }  // namespace eakv
@@ -292,7 +315,10 @@ int eakv_set_device(int device) {
 }
 
 int eakv_cache_device(const eakv_cache_t *c) { return c ? c->device : -1; }
-size_t eakv_cache_device_bytes(const eakv_cache_t *c) { return c ? c->buf_bytes : 0; }
+// The page slab plus the cache's scratch (host staging, split workspace).
+size_t eakv_cache_device_bytes(const eakv_cache_t *c) {
+  return c ? c->buf_bytes + (c->d_scratch ? c->scratch_bytes : 0) : 0;
+}
 void *eakv_cache_stream(const eakv_cache_t *c) { return c ? (void *)c->stream : nullptr; }
 
 int eakv_cache_set_stream(eakv_cache_t *c, void *stream) {

@@ -11,7 +11,9 @@
 // (cp.async.bulk, one per page) and consumes them with an online
 // (running-max) softmax. Each page is read from HBM exactly once and every
 // query head of the KV head is served from it (the GQA loop flip). Splits of
-// the same row are merged afterwards by an exact log-sum-exp combine.
+// the same row are merged by an exact log-sum-exp combine inside the same
+// launch: the last CTA of a row group to finish merges the group's splits
+// (decode_common.cuh), so a decode is always one kernel launch.
 //
 // Arithmetic (CUDA cores, packed f32x2 FMA):
 //   score_h(t) = s(t) * sum_i q'_h[i] n_i(t) + b(t) * sum_i q'_h[i]
@@ -107,7 +109,10 @@ decode_simt_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
   const int nhg = G / GC;
   if (!launch_ok(a) || G % GC != 0) return;
   const Item it = decode_item(a, batch, nhg);
-  if (!item_ok(a, it, it.h * G + it.hg * GC, GC)) return;
+  if (!item_ok(a, it, it.h * G + it.hg * GC, GC)) {
+    if (a.n_splits > 1 && !a.sep_merge) arrive_last(a);   // keeps the item's split counter in step
+    return;
+  }
   const size_t kv_stride = (size_t)a.geom.n_heads * a.geom.n_pages;   // pages from K to V
   const uint8_t *kpages =
       batch.base[it.b] + page_index(a.geom, it.layer, 0, it.h, 0) * C::PB;
@@ -185,7 +190,7 @@ decode_simt_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
     const int st = i % C::NSTAGE;
     if (!ok || !wait_requested(&last_req[st], i, a.wait_budget) ||
         !mbar_wait(smem_u32(&bars[st]), (i / C::NSTAGE) & 1, a.wait_budget)) {
-      atomicOr(a.status, kStatusWaitTimeout);
+      report(a, kStatusWaitTimeout);
       ok = false;
       break;
     }
@@ -286,12 +291,15 @@ decode_simt_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
   // every wait above is bounded, so all threads get here; leave together
   if (!__syncthreads_and(ok)) {
     if (threadIdx.x == 0) drain_stages(bars, last_req, C::NSTAGE, a.wait_budget);
+    // arrive without a record (the status word says why); if this CTA is
+    // the item's last, nothing is merged
+    if (a.n_splits > 1 && !a.sep_merge) arrive_last(a);
     return;
   }
   // every page requested was waited for, so no copy is in flight; checked,
   // and drained if not, before the ring is reused and the CTA exits
   if (threadIdx.x == 0 && !stages_idle(bars, last_req, C::NSTAGE)) {
-    atomicOr(a.status, kStatusLateCopy);
+    report(a, kStatusLateCopy);
     drain_stages(bars, last_req, C::NSTAGE, a.wait_budget);
   }
 
@@ -368,46 +376,43 @@ decode_simt_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
       }
     }
   }
-}
-
-// Merge the splits of each row: grid = rows, block = HD threads.
-__global__ void split_combine_kernel(const DecodeArgs a, int HD) {
-  const size_t row = blockIdx.x;
-  const int d = threadIdx.x;
-  const int ns = a.n_splits;
-  float M = -INFINITY;
-  for (int s = 0; s < ns; s++) M = fmaxf(M, a.part_m[row * ns + s]);
-  float O = 0.0f, L = 0.0f;
-  if (M != -INFINITY) {
-    for (int s = 0; s < ns; s++) {
-      const float f = ex2(a.part_m[row * ns + s] - M);
-      O = fmaf(f, a.part_o[(row * ns + s) * HD + d], O);
-      L = fmaf(f, a.part_l[row * ns + s], L);
-    }
-  }
-  a.out[row * HD + d] = O / L;
-  if (a.lse && d == 0) a.lse[row] = L > 0.0f ? (M + log2f(L)) * kLn2 : -INFINITY;
+  // the item's last split to finish merges all of them
+  if (a.n_splits > 1 && !a.sep_merge && arrive_last(a)) merge_splits<HD>(a, row0, GC);
 }
 
 // Exact merge of partial results given as (normalized output, natural LSE).
-__global__ void lse_combine_kernel(int n_parts, size_t n_rows, int HD, const float *parts,
-                                   const float *lse, float *out, float *lse_out) {
+// Part p's rows start at parts + p * part_stride and its LSEs at
+// lse + p * lse_stride (floats).
+__global__ void lse_combine_kernel(int n_parts, int HD, const float *parts, size_t part_stride,
+                                   const float *lse, size_t lse_stride, float *out,
+                                   float *lse_out) {
   const size_t row = blockIdx.x;
   const int d = threadIdx.x;
   float M = -INFINITY;
-  for (int p = 0; p < n_parts; p++) M = fmaxf(M, lse[p * n_rows + row]);
+  for (int p = 0; p < n_parts; p++) M = fmaxf(M, lse[p * lse_stride + row]);
   float O = 0.0f, L = 0.0f;
   if (M != -INFINITY) {
     for (int p = 0; p < n_parts; p++) {
-      const float lp = lse[p * n_rows + row];
+      const float lp = lse[p * lse_stride + row];
       if (lp == -INFINITY) continue;   // empty range: its output is 0/0
       const float f = ex2((lp - M) * kLog2e);
-      if (d < HD) O = fmaf(f, parts[(p * n_rows + row) * HD + d], O);
+      if (d < HD) O = fmaf(f, parts[p * part_stride + row * HD + d], O);
       L += f;
     }
   }
   if (d < HD) out[row * HD + d] = O / L;
   if (lse_out && d == 0) lse_out[row] = L > 0.0f ? M + logf(L) : -INFINITY;
+}
+
+// The split merge as a kernel of its own (grid = rows, block = HD threads):
+// what the decode kernels do in their last CTA of a row group, kept as a
+// second launch for the tests that compare the two bit for bit.
+__global__ void split_merge_kernel(const DecodeArgs a) {
+  if (a.head_dim == 128) {
+    if (threadIdx.x < 128) merge_row<128>(a, blockIdx.x, threadIdx.x);
+  } else {
+    if (threadIdx.x < 64) merge_row<64>(a, blockIdx.x, threadIdx.x);
+  }
 }
 
 typedef void (*DecodeFn)(const DecodeArgs, const DecodeBatch);
@@ -599,6 +604,12 @@ size_t decode_workspace_bytes(const DecodeArgs &a0, const DecodeBatch &batch) {
   return rows * a.n_splits * (size_t)(a.head_dim + 2) * sizeof(float);
 }
 
+size_t decode_counters(const DecodeArgs &a0, const DecodeBatch &batch) {
+  DecodeArgs a = a0;
+  const Plan p = plan(a, batch);
+  return a.n_splits > 1 ? (size_t)p.items : 0;
+}
+
 int decode_launch(const DecodeArgs &a0, const DecodeBatch &batch, void *workspace,
                   size_t workspace_bytes, cudaStream_t s) {
   DecodeArgs a = a0;
@@ -609,6 +620,10 @@ int decode_launch(const DecodeArgs &a0, const DecodeBatch &batch, void *workspac
     size_t need = rows * a.n_splits * (size_t)(a.head_dim + 2) * sizeof(float);
     if (!workspace || workspace_bytes < need) {
       set_error(EAKV_ERR_ALLOC, "decode: workspace too small (%zu < %zu)", workspace_bytes, need);
+      return EAKV_ERR_ALLOC;
+    }
+    if (!a.cnt && !a.sep_merge) {
+      set_error(EAKV_ERR_ALLOC, "decode: no split counters");
       return EAKV_ERR_ALLOC;
     }
     a.part_o = (float *)workspace;
@@ -623,20 +638,20 @@ int decode_launch(const DecodeArgs &a0, const DecodeBatch &batch, void *workspac
   else
     rc = a.head_dim == 128 ? dispatch_gc<128>(p.gc, a, batch, n_blocks, s)
                            : dispatch_gc<64>(p.gc, a, batch, n_blocks, s);
-  if (rc) return rc;
-  if (a.n_splits > 1) {
-    size_t rows = (size_t)a.n_caches * a.n_layers * a.n_q_heads;
-    split_combine_kernel<<<(unsigned)rows, a.head_dim, 0, s>>>(a, a.head_dim);
-    rc = check_cuda(cudaGetLastError(), "decode: combine launch");
+  if (!rc && a.n_splits > 1 && a.sep_merge) {
+    const size_t rows = (size_t)a.n_caches * a.n_layers * a.n_q_heads;
+    split_merge_kernel<<<(unsigned)rows, a.head_dim, 0, s>>>(a);
+    rc = check_cuda(cudaGetLastError(), "decode: merge launch");
   }
   return rc;
 }
 
 int lse_combine_launch(int n_parts, int n_rows, int head_dim, const float *parts,
-                       const float *lse, float *out, float *lse_out, cudaStream_t s) {
+                       size_t part_stride, const float *lse, size_t lse_stride, float *out,
+                       float *lse_out, cudaStream_t s) {
   if (n_rows <= 0) return EAKV_OK;
-  lse_combine_kernel<<<n_rows, head_dim, 0, s>>>(n_parts, (size_t)n_rows, head_dim, parts, lse,
-                                                 out, lse_out);
+  lse_combine_kernel<<<n_rows, head_dim, 0, s>>>(n_parts, head_dim, parts, part_stride, lse,
+                                                 lse_stride, out, lse_out);
   return check_cuda(cudaGetLastError(), "lse_combine launch");
 }
 

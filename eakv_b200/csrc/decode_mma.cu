@@ -194,7 +194,10 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
   const int nhg = G / gh;
   if (!launch_ok(a) || gh < 1 || gh > RH || G % gh != 0) return;
   const Item it = decode_item(a, batch, nhg);
-  if (!item_ok(a, it, it.h * G + it.hg * gh, gh)) return;
+  if (!item_ok(a, it, it.h * G + it.hg * gh, gh)) {
+    if (a.n_splits > 1 && !a.sep_merge) arrive_last(a);   // keeps the item's split counter in step
+    return;
+  }
   const size_t kv_stride = (size_t)a.geom.n_heads * a.geom.n_pages;
   const uint8_t *kpages = batch.base[it.b] + page_index(a.geom, it.layer, 0, it.h, 0) * C::PB;
   const uint8_t *vpages = kpages + kv_stride * C::PB;
@@ -484,7 +487,7 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
     const int st = i % C::NSTAGE;
     if (!ok || !wait_requested(&last_req[st], i, a.wait_budget) ||
         !mbar_wait(smem_u32(&bars[st]), (i / C::NSTAGE) & 1, a.wait_budget)) {
-      atomicOr(a.status, kStatusWaitTimeout);
+      report(a, kStatusWaitTimeout);
       ok = false;
       break;
     }
@@ -519,12 +522,15 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
   }
   if (!__syncthreads_and(ok)) {
     if (threadIdx.x == 0) drain_stages(bars, last_req, C::NSTAGE, a.wait_budget);
+    // arrive without a record (the status word says why); if this CTA is
+    // the item's last, nothing is merged
+    if (a.n_splits > 1 && !a.sep_merge) arrive_last(a);
     return;
   }
   // every page requested was waited for, so no copy is in flight; checked,
   // and drained if not, before the ring is reused and the CTA exits
   if (threadIdx.x == 0 && !stages_idle(bars, last_req, C::NSTAGE)) {
-    atomicOr(a.status, kStatusLateCopy);
+    report(a, kStatusLateCopy);
     drain_stages(bars, last_req, C::NSTAGE, a.wait_budget);
   }
 
@@ -606,6 +612,8 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
       }
     }
   }
+  // the item's last split to finish merges all of them
+  if (a.n_splits > 1 && !a.sep_merge && arrive_last(a)) merge_splits<HD>(a, row0, gh);
 }
 
 template <int HD, int RH>

@@ -79,9 +79,12 @@ struct eakv_cache {
   int device;
   cudaStream_t stream;
   int own_stream;
-  // grow-on-demand device scratch for the host-pointer entry points
+  // grow-on-demand device scratch for the host-pointer entry points and the
+  // decode's split workspace: [cnt_bytes of u32 split counters, kept at
+  // zero between calls | data]. scratch_bytes is the whole allocation.
   mutable void *d_scratch;
   mutable size_t scratch_bytes;
+  mutable size_t cnt_bytes;
 };
 
 namespace eakv {
@@ -105,7 +108,14 @@ struct DeviceGuard {
   }
 };
 
-void *cache_scratch(const eakv_cache *c, size_t bytes);   // nullptr on failure
+// Data space of at least `bytes` in the cache's scratch (nullptr on failure).
+// Growing it synchronizes the cache's stream and reallocates.
+void *cache_scratch(const eakv_cache *c, size_t bytes);
+// The same data space plus at least n_counters u32 counters that are zero
+// at every call boundary (the decode kernels return each counter to zero).
+// Both pointers come from one allocation, so one call gives both.
+int cache_workspace(const eakv_cache *c, size_t n_counters, size_t bytes, unsigned **counters,
+                    void **data);
 
 // ---- quantize.cu ----
 // Quantizes n_units units of n_tok*head_dim floats each: the n_tok*gpd
@@ -149,6 +159,11 @@ struct DecodeArgs {
                                     // requested, so its wait runs out (tests only)
   int fix_split_pages, fix_n_splits;  // > 0: keep this split plan (one chunk of a
                                       // batch that was planned as a whole)
+  // split merge: one counter per work item (row group) when rows are
+  // split; the last CTA of an item to finish merges its splits and returns
+  // the counter to zero
+  unsigned *cnt;
+  int sep_merge;                    // 1: merge the splits in a second kernel instead (tests)
   // filled by the planner
   int n_splits, split_pages;
   int cta_heads;                    // tensor-core path: query heads per CTA
@@ -157,6 +172,9 @@ struct DecodeArgs {
 int decode_launch(const DecodeArgs &a, const DecodeBatch &batch, void *workspace,
                   size_t workspace_bytes, cudaStream_t s);
 size_t decode_workspace_bytes(const DecodeArgs &a, const DecodeBatch &batch);
+// Split counters a decode launch needs (one per work item when rows are
+// split, else 0); a.cnt must point at that many zeroed counters.
+size_t decode_counters(const DecodeArgs &a, const DecodeBatch &batch);
 // Plans `a` over the whole batch and records the split plan in
 // a.fix_split_pages / a.fix_n_splits, so that chunks of it launched on their
 // own keep the same splits.
@@ -164,9 +182,18 @@ void decode_fix_plan(DecodeArgs &a, const DecodeBatch &batch);
 // The planner's split count for `items` rows of max_pages pages, searched in
 // [lo, hi], per_sm CTAs resident on each of `sms` SMs (host code only).
 int choose_splits(long long items, int max_pages, int lo, int hi, int per_sm, int sms);
+// Part p of the merge reads rows at parts + p * part_stride and LSEs at
+// lse + p * lse_stride (floats).
 int lse_combine_launch(int n_parts, int n_rows, int head_dim, const float *parts,
-                       const float *lse, float *out, float *lse_out, cudaStream_t s);
+                       size_t part_stride, const float *lse, size_t lse_stride, float *out,
+                       float *lse_out, cudaStream_t s);
 int *device_status_ptr();   // status word of the current device
+// Shared by the decode entry points (api.cu): argument checks of a batch of
+// caches, the default launch arguments (after the device guard: they hold
+// the current device's status word), and the per-cache table of a batch.
+int check_batch(const eakv_cache_t *const *caches, int n, int n_q, const char *who);
+DecodeArgs base_args(const eakv_cache_t *c0, int n_caches, int n_q);
+void fill_batch(DecodeBatch &b, const eakv_cache_t *const *caches, int n);
 // decode_mma.cu: tensor-core decode, any number of query heads per KV head
 int mma_heads_per_cta(int G, int head_dim);   // 0 when the head_dim is not served
 int mma_resident(int gh, int head_dim);
@@ -174,6 +201,7 @@ int mma_launch(int gh, const DecodeArgs &a, const DecodeBatch &b, int n_blocks, 
 extern thread_local int t_force_path;
 extern thread_local int t_force_splits;
 extern thread_local int t_test_stall;
+extern thread_local int t_sep_merge;
 extern thread_local unsigned t_wait_budget;
 
 }  // namespace eakv

@@ -1,0 +1,232 @@
+// split.cu - the multi-GPU decode of one long context over NCCL.
+//
+// The reference decodes a sequence in one serial loop over positions on one
+// CPU core (kernels/fused_k_score_gqa.ea:29, kernels/fused_attention.ea:
+// 38-187). Across GPUs the work is partitioned two ways:
+//
+// * KV-head shards: each GPU holds some KV heads (with their query heads) of
+//   every sequence and layer. Heads are independent; there is no exchange,
+//   and a shard calls the ordinary batched decode.
+// * Sequence split: each GPU of a group holds a slice of the positions of
+//   every sequence. eakv_decode_attention_split runs, on one stream,
+//     1. the partial decode of the local slice, writing this rank's record
+//        (normalized output, natural-log LSE) of every row into its slot of
+//        a packed buffer [rank][rows x head_dim outputs | rows LSEs];
+//     2. one in-place ncclAllGather of that buffer over the group's
+//        communicator: the records are the only bytes that cross NVLink;
+//     3. the exact merge of the group's records on every rank:
+//        out = sum_r exp(lse_r - L) out_r, L = log sum_r exp(lse_r).
+//   Softmax attention over a set of positions does not depend on their
+//   order, so a rank's slice can sit at local positions 0.. of its caches.
+//
+// NCCL is resolved at run time (dlopen of libnccl.so.2, preferring a copy
+// the process already has loaded, e.g. by a framework), so the library
+// loads and its other entry points work where NCCL is absent; a
+// communicator passed in must come from that same NCCL. Errors come back as
+// EAKV_ERR_INVALID with NCCL's message in eakv_last_error_string().
+#include <dlfcn.h>
+#include <nccl.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "internal.cuh"
+
+namespace eakv {
+namespace {
+
+struct NcclApi {
+  decltype(&ncclGetUniqueId) get_unique_id = nullptr;
+  decltype(&ncclCommInitRank) comm_init_rank = nullptr;
+  decltype(&ncclCommDestroy) comm_destroy = nullptr;
+  decltype(&ncclCommAbort) comm_abort = nullptr;
+  decltype(&ncclAllGather) all_gather = nullptr;
+  decltype(&ncclGetErrorString) error_string = nullptr;
+  decltype(&ncclCommCount) comm_count = nullptr;
+  decltype(&ncclCommUserRank) comm_user_rank = nullptr;
+  decltype(&ncclCommCuDevice) comm_cu_device = nullptr;
+  decltype(&ncclGetVersion) get_version = nullptr;
+  bool loaded = false;
+  char why[160] = "";
+};
+
+template <typename F>
+bool bind(void *h, F &fn, const char *name, NcclApi &n) {
+  fn = reinterpret_cast<F>(dlsym(h, name));
+  if (!fn) snprintf(n.why, sizeof n.why, "NCCL library lacks %s", name);
+  return fn != nullptr;
+}
+
+// The process's NCCL, loaded once: EAKV_NCCL_LIB if set, else a
+// libnccl.so.2 already loaded, else the dynamic linker's search.
+const NcclApi *nccl(const char *who) {
+  static NcclApi n;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *h = nullptr;
+    const char *env = getenv("EAKV_NCCL_LIB");
+    if (env && *env) h = dlopen(env, RTLD_NOW | RTLD_LOCAL);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    if (!h) {
+      snprintf(n.why, sizeof n.why, "libnccl.so.2 not found (%s)", dlerror());
+      return;
+    }
+    n.loaded = bind(h, n.get_unique_id, "ncclGetUniqueId", n) &&
+               bind(h, n.comm_init_rank, "ncclCommInitRank", n) &&
+               bind(h, n.comm_destroy, "ncclCommDestroy", n) &&
+               bind(h, n.comm_abort, "ncclCommAbort", n) &&
+               bind(h, n.all_gather, "ncclAllGather", n) &&
+               bind(h, n.error_string, "ncclGetErrorString", n) &&
+               bind(h, n.comm_count, "ncclCommCount", n) &&
+               bind(h, n.comm_user_rank, "ncclCommUserRank", n) &&
+               bind(h, n.comm_cu_device, "ncclCommCuDevice", n) &&
+               bind(h, n.get_version, "ncclGetVersion", n);
+  });
+  if (!n.loaded) {
+    set_error(EAKV_ERR_INVALID, "%s: NCCL unavailable: %s", who, n.why);
+    return nullptr;
+  }
+  return &n;
+}
+
+int check_nccl(const NcclApi *n, ncclResult_t r, const char *what) {
+  if (r == ncclSuccess) return EAKV_OK;
+  set_error(EAKV_ERR_INVALID, "%s: %s", what, n->error_string(r));
+  return EAKV_ERR_INVALID;
+}
+
+// Floats of one rank's record block: rows outputs of head_dim, then rows
+// LSEs, padded to 64 floats so every rank's block starts 256-byte aligned.
+size_t record_floats(size_t rows, int head_dim) {
+  return (rows * (head_dim + 1) + 63) / 64 * 64;
+}
+
+}  // namespace
+}  // namespace eakv
+
+using namespace eakv;
+
+extern "C" {
+
+int eakv_nccl_version(void) {
+  clear_error();
+  const NcclApi *n = nccl("nccl_version");
+  if (!n) return EAKV_ERR_INVALID;
+  int v = 0;
+  int rc = check_nccl(n, n->get_version(&v), "nccl_version");
+  return rc ? rc : v;
+}
+
+int eakv_nccl_unique_id(void *id) {
+  clear_error();
+  if (!id) {
+    set_error(EAKV_ERR_INVALID, "nccl_unique_id: NULL buffer");
+    return EAKV_ERR_INVALID;
+  }
+  const NcclApi *n = nccl("nccl_unique_id");
+  if (!n) return EAKV_ERR_INVALID;
+  ncclUniqueId u;
+  int rc = check_nccl(n, n->get_unique_id(&u), "ncclGetUniqueId");
+  if (rc) return rc;
+  memcpy(id, &u, sizeof u);
+  return EAKV_OK;
+}
+
+int eakv_nccl_comm_init(void **comm, int n_ranks, const void *id, int rank, int device) {
+  clear_error();
+  if (!comm || !id || n_ranks < 1 || rank < 0 || rank >= n_ranks || device < 0) {
+    set_error(EAKV_ERR_INVALID, "nccl_comm_init: invalid argument");
+    return EAKV_ERR_INVALID;
+  }
+  const NcclApi *n = nccl("nccl_comm_init");
+  if (!n) return EAKV_ERR_INVALID;
+  DeviceGuard g(device);
+  ncclUniqueId u;
+  memcpy(&u, id, sizeof u);
+  ncclComm_t c = nullptr;
+  int rc = check_nccl(n, n->comm_init_rank(&c, n_ranks, u, rank), "ncclCommInitRank");
+  if (rc) return rc;
+  *comm = c;
+  return EAKV_OK;
+}
+
+int eakv_nccl_comm_destroy(void *comm) {
+  clear_error();
+  if (!comm) return EAKV_OK;
+  const NcclApi *n = nccl("nccl_comm_destroy");
+  if (!n) return EAKV_ERR_INVALID;
+  return check_nccl(n, n->comm_destroy((ncclComm_t)comm), "ncclCommDestroy");
+}
+
+int eakv_nccl_comm_abort(void *comm) {
+  clear_error();
+  if (!comm) return EAKV_OK;
+  const NcclApi *n = nccl("nccl_comm_abort");
+  if (!n) return EAKV_ERR_INVALID;
+  return check_nccl(n, n->comm_abort((ncclComm_t)comm), "ncclCommAbort");
+}
+
+int eakv_decode_attention_split(const eakv_cache_t *const *caches, int n_caches,
+                                const float *d_q, int n_q, int pos_begin, int pos_end,
+                                float *d_out, void *comm, void *stream) {
+  clear_error();
+  const char *who = "decode_attention_split";
+  int rc = check_batch(caches, n_caches, n_q, who);
+  if (rc) return rc;
+  if (!d_q || !d_out || !comm || pos_begin < 0 || (pos_end >= 0 && pos_end < pos_begin)) {
+    set_error(EAKV_ERR_INVALID, "%s: invalid argument", who);
+    return EAKV_ERR_INVALID;
+  }
+  const NcclApi *n = nccl(who);
+  if (!n) return EAKV_ERR_INVALID;
+  ncclComm_t nc = (ncclComm_t)comm;
+  int world = 0, rank = 0, cdev = -1;
+  rc = check_nccl(n, n->comm_count(nc, &world), "ncclCommCount");
+  if (!rc) rc = check_nccl(n, n->comm_user_rank(nc, &rank), "ncclCommUserRank");
+  if (!rc) rc = check_nccl(n, n->comm_cu_device(nc, &cdev), "ncclCommCuDevice");
+  if (rc) return rc;
+  const eakv_cache_t *c0 = caches[0];
+  if (cdev != c0->device) {
+    set_error(EAKV_ERR_INVALID, "%s: communicator on device %d, caches on device %d", who, cdev,
+              c0->device);
+    return EAKV_ERR_INVALID;
+  }
+  DeviceGuard g(c0->device);
+  cudaStream_t s = stream ? (cudaStream_t)stream : c0->stream;
+  DecodeArgs a = base_args(c0, n_caches, n_q);
+  if (!a.status) {
+    set_error(EAKV_ERR_INVALID, "%s: device status word unavailable", who);
+    return EAKV_ERR_INVALID;
+  }
+  a.q = d_q;
+  a.pos_begin = pos_begin;
+  a.pos_end = pos_end;
+  DecodeBatch b;
+  fill_batch(b, caches, n_caches);
+  const int hd = c0->head_dim;
+  const size_t rows = (size_t)n_caches * c0->n_layers * n_q;
+  const size_t rec = record_floats(rows, hd);
+  // scratch: [records of every rank | decode split workspace]
+  const size_t rec_bytes = (size_t)world * rec * sizeof(float);
+  const size_t ws = decode_workspace_bytes(a, b);
+  void *base = nullptr;
+  rc = cache_workspace(c0, decode_counters(a, b), rec_bytes + ws, &a.cnt, &base);
+  if (rc) return rc;
+  float *records = (float *)base;
+  float *mine = records + (size_t)rank * rec;
+  a.out = mine;
+  a.lse = mine + rows * hd;
+  rc = decode_launch(a, b, ws ? (uint8_t *)base + rec_bytes : nullptr, ws, s);
+  if (rc) return rc;
+  if (world > 1) {
+    rc = check_nccl(n, n->all_gather(mine, records, rec, ncclFloat32, nc, s), "ncclAllGather");
+    if (rc) return rc;
+  }
+  return lse_combine_launch(world, (int)rows, hd, records, rec, records + rows * hd, rec, d_out,
+                            nullptr, s);
+}
+
+}  // extern "C"

@@ -2,27 +2,27 @@
 
 Two ways to spread the work:
 
-* Independent sequences (the default): each rank owns whole sequences and
-  decodes them with `eakv_decode_attention`; no data-path collective.
+* KV-head shards: each rank holds some KV heads (with their query heads)
+  of every sequence and layer and decodes them with `eakv_decode_attention`;
+  heads are independent, so there is no data-path collective.
 * Sequence split, for a context larger than one GPU's share: rank r holds
-  positions [begin_r, end_r) of every sequence in its own local caches,
-  computes that range's normalized output and natural-log LSE with
-  `eakv_decode_attention_partial`, the ranks all-gather (output, LSE), and
-  `eakv_lse_combine` merges them exactly:
+  positions [begin_r, end_r) of every sequence in its own local caches, and
+  `eakv_decode_attention_split` (include/eakv_nccl.h) computes that range's
+  record (normalized output, natural-log LSE), all-gathers the records of
+  the group over the library's own NCCL communicator and merges them
+  exactly, all on one CUDA stream:
 
       out = sum_r exp(lse_r - L) out_r,   L = log sum_r exp(lse_r).
 
 Softmax attention over a set of positions does not depend on their order,
 so a rank's slice can sit at local positions 0.. of its caches.
 
-torch.distributed is the plumbing (NCCL on GPUs, gloo on CPU for the
-tests); the kernels are the library's.
+torch.distributed is only the launcher's plumbing here (it carries the NCCL
+unique id to the ranks of a group); the data path is the library's.
 """
 import math
 
 import numpy as np
-
-from . import decode_attention_partial, lse_combine
 
 PAGE = 64
 
@@ -79,43 +79,38 @@ def merge_partials_np(outs, lses):
 
 
 class SeqSplitDecoder:
-    """Sequence-split decode over a torch.distributed process group.
+    """Sequence-split decode over one group of ranks, through the library.
 
-    caches: this rank's local caches (its slice of every sequence).
-    Every rank calls `step` with the same queries; every rank receives the
-    merged output. Collectives are issued in the same order on all ranks.
+    caches: this rank's local caches (its slice of every sequence). The
+    group's first rank makes an NCCL unique id, torch.distributed carries it
+    to the others, and every rank joins the library's communicator on
+    `device` (collective: every rank of the group constructs its decoder at
+    the same point). Every rank calls `step` with the same queries, in the
+    same order; every rank receives the merged output.
     """
 
-    def __init__(self, caches, n_q_heads, head_dim, group=None):
-        import torch
+    def __init__(self, caches, n_q_heads, head_dim, group=None, device=None):
         import torch.distributed as dist
-        self.dist = dist
-        self.torch = torch
+        from . import NcclComm, nccl_unique_id
         self.caches = caches
         self.n_q = n_q_heads
         self.hd = head_dim
-        self.group = group
         self.world = dist.get_world_size(group)
-        self.rows = len(caches) * caches[0].n_layers * n_q_heads
+        rank = dist.get_rank(group)
+        leader = dist.get_global_rank(group, 0) if group is not None else 0
+        box = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=leader, group=group)
+        dev = caches[0].device if device is None else device
+        self.comm = NcclComm(self.world, box[0], rank, dev)
 
     def step(self, d_q, d_out, stream=None):
-        """One decode step. `stream` is a torch.cuda.Stream (a private one is
-        made if None): the partial kernel, the all-gathers and the merge are
-        all ordered on it, so nothing here synchronizes the host."""
-        torch, dist = self.torch, self.dist
-        dev = d_q.device
-        if stream is None:
-            if getattr(self, "_stream", None) is None:
-                self._stream = torch.cuda.Stream(dev)
-            stream = self._stream
-        with torch.cuda.stream(stream):
-            h = stream.cuda_stream
-            part = torch.empty(self.rows, self.hd, device=dev, dtype=torch.float32)
-            lse = torch.empty(self.rows, device=dev, dtype=torch.float32)
-            decode_attention_partial(self.caches, d_q, self.n_q, 0, -1, part, lse, stream=h)
-            parts = torch.empty(self.world, self.rows, self.hd, device=dev, dtype=torch.float32)
-            lses = torch.empty(self.world, self.rows, device=dev, dtype=torch.float32)
-            dist.all_gather_into_tensor(parts, part, group=self.group)
-            dist.all_gather_into_tensor(lses, lse, group=self.group)
-            lse_combine(self.world, self.rows, self.hd, parts, lses, d_out, None, stream=h)
+        """One decode step: `stream` is a CUDA stream handle (int) or a
+        torch.cuda.Stream; the partial decode, the all-gather and the merge
+        are all queued on it, and nothing synchronizes the host."""
+        from . import decode_attention_split
+        h = getattr(stream, "cuda_stream", stream)
+        decode_attention_split(self.caches, d_q, self.n_q, d_out, self.comm, stream=h)
         return d_out
+
+    def close(self):
+        self.comm.destroy()

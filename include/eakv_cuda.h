@@ -48,7 +48,9 @@ int eakv_device_status(int device, int reset);
 int    eakv_set_device(int device);
 
 int    eakv_cache_device(const eakv_cache_t *cache);         /* -1 for NULL */
-size_t eakv_cache_device_bytes(const eakv_cache_t *cache);   /* HBM held */
+/* HBM held by the cache: its page slab plus the scratch that host-buffer
+ * calls and split decodes grow on demand. */
+size_t eakv_cache_device_bytes(const eakv_cache_t *cache);
 /* Stream used by this cache's calls; NULL restores the cache's own. */
 int    eakv_cache_set_stream(eakv_cache_t *cache, void *stream);
 void  *eakv_cache_stream(const eakv_cache_t *cache);
@@ -122,9 +124,15 @@ int eakv_decode_attention_host(const eakv_cache_t *const *caches,
                                int n_q_heads, float *output, void *stream);
 
 /* Number of kernel launches one eakv_decode_attention call over these
- * caches makes (1, or 2 when rows are split and merged); < 0 on error. */
+ * caches makes: 1 (rows cut into sequence splits are merged inside the same
+ * launch by the last CTA of each row group); < 0 on error. */
 int eakv_decode_launches(const eakv_cache_t *const *caches, int n_caches,
                          int n_q_heads);
+/* Sequence splits per row the planner chooses for one eakv_decode_attention
+ * call over these caches (1: rows are not split and no split workspace is
+ * used); < 0 on error. */
+int eakv_decode_splits(const eakv_cache_t *const *caches, int n_caches,
+                       int n_q_heads);
 
 /* ---- sequence-split partials and exact combine ----------------------- */
 
@@ -187,6 +195,12 @@ int eakv_test_choose_splits(long long items, int max_pages, int lo, int hi, int 
  * groups of 4 or 8); 0 restores the automatic choice. For tests and
  * side-by-side measurements. */
 int eakv_test_force_path(int path);
+
+/* on != 0 makes later decode calls on this host thread merge their sequence
+ * splits in a second kernel launch after the decode, instead of in the
+ * decode kernel's last CTA of each row group; 0 restores the default. The
+ * arithmetic is the same; tests compare the two bit for bit. */
+int eakv_test_separate_merge(int on);
 
 /* Failure-detection test: later fused / decode calls on this host thread
  * never request page `page` of each (row, split) work item into the

@@ -65,6 +65,9 @@ def olib():
         for n in ("q4_k_score_gqa_f32", "q4_k_score_gqa_64_f32", "q4_v_sum_gqa_f32",
                   "q4_v_sum_gqa_64_f32"):
             getattr(L, n).argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, _I]
+        for n in ("q4_fused_k_score_f32", "q4_fused_k_score_64_f32", "q4_fused_v_sum_f32",
+                  "q4_fused_v_sum_64_f32"):
+            getattr(L, n).argtypes = [_P, _P, _P, _P, _P, _I, _I]
         L.q4_fused_attention_multi_f32.argtypes = [_P] * 8 + [_I, _I, _I]
         L.oracle_fused_attention.argtypes = [_P] * 8 + [_I, _I, _I, _I, _I]
         L.q4_validate.argtypes = [_P, _P, _P, _P, _I]
@@ -250,6 +253,27 @@ class RefCache:
                           np.ascontiguousarray(vb[g:]))
         olib().oracle_fused_attention(ptr(q), ptr(kw), ptr(ks), ptr(kb), ptr(vw), ptr(vs),
                                       ptr(vb), ptr(out), hi - lo, n_q, n_kv, self.gph, self.hd)
+        return out
+
+    def scores_single(self, q, layer, head):
+        """Scores of one query vector against KV head `head` through the
+        reference's single-head kernel with a group offset
+        (kernels/fused_k_score.ea:9-153, fused_k_score_64.ea:5-94)."""
+        q = np.ascontiguousarray(q, np.float32)
+        out = np.zeros(self.seq_len, np.float32)
+        w, s, b = self._blk(layer, 0)
+        fn = olib().q4_fused_k_score_64_f32 if self.hd == 64 else olib().q4_fused_k_score_f32
+        fn(ptr(q), ptr(w), ptr(s), ptr(b), ptr(out), self.seq_len, head * self.gph)
+        return out
+
+    def output_single(self, wts, layer, head):
+        """V sum of one weight row over KV head `head` through the reference's
+        single-head kernel (kernels/fused_v_sum.ea:7-77, fused_v_sum_64.ea:5-50)."""
+        wts = np.ascontiguousarray(wts, np.float32)
+        out = np.zeros(self.hd, np.float32)
+        w, s, b = self._blk(layer, 1)
+        fn = olib().q4_fused_v_sum_64_f32 if self.hd == 64 else olib().q4_fused_v_sum_f32
+        fn(ptr(wts), ptr(w), ptr(s), ptr(b), ptr(out), self.seq_len, head * self.gph)
         return out
 
     def dequant_head(self, layer, kv, h):

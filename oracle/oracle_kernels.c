@@ -272,6 +272,36 @@ HOT void q4_k_score_gqa_64_f32(const float *q_vecs, const uint8_t *k_packed,
                 n_q_heads, n_kv_heads, groups_per_head, 64);
 }
 
+/* Single-head forms with a group offset (the caller passes the raw block and
+ * the head's first group): fused_k_score.ea:9-153 (head_dim 128, two
+ * positions per trip) and fused_k_score_64.ea:5-94. Each position is its own
+ * 16-lane chain and reduce_add, so one position at a time gives the same
+ * bits as the reference's two-position unrolling. Not called by the
+ * reference's host code (src/attention.c uses the _multi and _gqa forms). */
+static void k_score_single(const float *q_vec, const uint8_t *k_packed, const float *k_scales,
+                           const float *k_biases, float *scores, int32_t seq_len,
+                           int32_t group_offset, int hd) {
+    const int gpd = hd / 64;
+    const float rsqrt_d = 1.0f / sqrtf((float)hd);
+    for (int32_t t = 0; t < seq_len; t++) {
+        int64_t g0 = (int64_t)group_offset + (int64_t)t * gpd;
+        scores[t] = score_one(q_vec, k_packed + g0 * 32, k_scales + g0, k_biases + g0, gpd,
+                              rsqrt_d);
+    }
+}
+
+HOT void q4_fused_k_score_f32(const float *q_vec, const uint8_t *k_packed,
+                              const float *k_scales, const float *k_biases, float *scores,
+                              int32_t seq_len, int32_t group_offset) {
+    k_score_single(q_vec, k_packed, k_scales, k_biases, scores, seq_len, group_offset, 128);
+}
+
+HOT void q4_fused_k_score_64_f32(const float *q_vec, const uint8_t *k_packed,
+                                 const float *k_scales, const float *k_biases, float *scores,
+                                 int32_t seq_len, int32_t group_offset) {
+    k_score_single(q_vec, k_packed, k_scales, k_biases, scores, seq_len, group_offset, 64);
+}
+
 /* ---------------------------------------------------------------------
  * V-sum. Every output element is its own chain over positions in order:
  * o = fma(fma(n, s, b), w[q_h, t], o), o starting at 0
@@ -336,6 +366,43 @@ static void v_sum_gqa(const float *all_weights, const uint8_t *v_packed,
 #endif
         }
     }
+}
+
+/* Single-head V sums with a group offset: fused_v_sum.ea:7-77 (head_dim
+ * 128) and fused_v_sum_64.ea:5-50. out[d] = chain over t of
+ * fma(fma(n, s, b), weights[t], .), element by element, as the vector
+ * accumulators o0..o7 run it. */
+static void v_sum_single(const float *weights, const uint8_t *v_packed, const float *v_scales,
+                         const float *v_biases, float *out_vec, int32_t seq_len,
+                         int32_t group_offset, int hd) {
+    const int gpd = hd / 64;
+    float o[128];
+    for (int d = 0; d < hd; d++) o[d] = 0.0f;
+    for (int32_t t = 0; t < seq_len; t++) {
+        for (int g = 0; g < gpd; g++) {
+            int64_t gi = (int64_t)group_offset + (int64_t)t * gpd + g;
+            const uint8_t *p = v_packed + gi * 32;
+            float s = v_scales[gi], b = v_biases[gi];
+            for (int k = 0; k < 32; k++) {
+                o[g * 64 + k] = fmaf(fmaf(lo_nib(p, k), s, b), weights[t], o[g * 64 + k]);
+                o[g * 64 + 32 + k] =
+                    fmaf(fmaf(hi_nib(p, k), s, b), weights[t], o[g * 64 + 32 + k]);
+            }
+        }
+    }
+    memcpy(out_vec, o, (size_t)hd * sizeof(float));
+}
+
+HOT void q4_fused_v_sum_f32(const float *weights, const uint8_t *v_packed,
+                            const float *v_scales, const float *v_biases, float *out_vec,
+                            int32_t seq_len, int32_t group_offset) {
+    v_sum_single(weights, v_packed, v_scales, v_biases, out_vec, seq_len, group_offset, 128);
+}
+
+HOT void q4_fused_v_sum_64_f32(const float *weights, const uint8_t *v_packed,
+                               const float *v_scales, const float *v_biases, float *out_vec,
+                               int32_t seq_len, int32_t group_offset) {
+    v_sum_single(weights, v_packed, v_scales, v_biases, out_vec, seq_len, group_offset, 64);
 }
 
 /* fused_v_sum.ea:83-163 */

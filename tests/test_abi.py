@@ -10,7 +10,7 @@ import pytest
 from conftest import ROOT
 
 HEADERS = [os.path.join(ROOT, "include", h)
-           for h in ("eakv.h", "eakv_cuda.h", "eakv_ggml.h", "eakv_llama.h")]
+           for h in ("eakv.h", "eakv_cuda.h", "eakv_ggml.h", "eakv_llama.h", "eakv_nccl.h")]
 
 
 def declared_functions():

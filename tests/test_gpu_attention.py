@@ -136,3 +136,27 @@ def test_unsupported_head_dim_rejected(gpu):
         assert c.load_raw(np.ones((1, 2, 2, 16, 256), np.float32), 16) == 0
         s = c.scores(np.ones(2 * 256, np.float32), 0, 2, 2)
         assert np.isnan(s).all() and E.last_error()[0] == E.EAKV_ERR_INVALID
+
+
+@pytest.mark.parametrize("hd,S,maxS", [(128, 301, 320), (64, 511, 512), (128, 64, 64)])
+def test_single_head_cache_against_single_head_kernels(gpu, hd, S, maxS):
+    """Row a10: a one-head cache (n_q = n_kv = 1) through the library's
+    two-call API and its fused decode, against the reference's single-head
+    kernels restated in the oracle (kernels/fused_k_score.ea:9-153,
+    fused_v_sum.ea:7-77 and the _64 forms): scores and V sum bit for bit
+    (one chunk), the fused path within 1e-4."""
+    rng = np.random.default_rng(hd + S)
+    L = 2
+    data = kv_data(rng, L, 1, S, hd)
+    rc = O.RefCache(L, 1, hd, maxS)
+    rc.load_raw(data, S)
+    with E.Cache(L, 1, hd, maxS) as c:
+        assert c.load_raw(data, S) == 0
+        for l in range(L):
+            q = rng.standard_normal(hd).astype(np.float32)
+            s_ref = rc.scores_single(q, l, 0)
+            assert np.array_equal(bits(c.scores(q, l, 1, 1)), bits(s_ref)), "scores"
+            w = O.softmax_rows(s_ref, 1, S)
+            assert np.array_equal(bits(c.output(w, l, 1, 1)), bits(rc.output_single(w, l, 0))), \
+                "V sum"
+            assert_close(c.fused(q, l, 1, 1), rc.fused(q, l, 1, 1), what=f"fused layer {l}")

@@ -273,3 +273,50 @@ def test_query_magnitudes(gpu, qscale):
     with E.Cache(L, nkv, hd, S) as c:
         assert c.load_raw(data, S) == 0
         assert_close(c.fused(q, 0, nq, nkv), rc.fused(q, 0, nq, nkv), what=f"q x{qscale}")
+
+
+@pytest.mark.parametrize("path", PATHS)
+@pytest.mark.parametrize("L,nq,nkv,hd,lens,splits", [
+    (2, 32, 8, 128, [3000, 1, 640, 2999], 0),   # planner's splits, ragged batch
+    (3, 64, 8, 128, [1300, 700], 5),             # 8 heads per CTA
+    (2, 32, 4, 64, [2048], 7),                   # head_dim 64, 8:1
+    (1, 8, 8, 128, [2048, 100], 3),              # MHA (one live head of four)
+    (1, 12, 4, 128, [999], 4),                   # ratio 3
+])
+def test_split_merge_in_kernel_equals_separate_pass(gpu, path, L, nq, nkv, hd, lens, splits):
+    """The last CTA of a row group merges the group's splits inside the decode
+    launch; a second kernel doing the same merge after the decode gives the
+    same bits. Three calls in a row: every call returns the split counters to
+    zero, so each call merges exactly once per row group."""
+    import torch
+    E.force_path(1 if path == "simt" else 0)
+    rng = np.random.default_rng(sum(lens) + nq)
+    maxS = max(lens)
+    caches = []
+    for n in lens:
+        c = E.Cache(L, nkv, hd, maxS)
+        assert c.load_raw(kv_data(rng, L, nkv, n, hd), n) == 0
+        caches.append(c)
+    E.force_splits(splits)
+    try:
+        assert E.decode_splits(caches, nq) > 1
+        assert E.decode_launches(caches, nq) == 1
+        for call in range(3):
+            q = torch.from_numpy(
+                rng.standard_normal((len(lens), L, nq, hd)).astype(np.float32)).to(gpu)
+            one = torch.full_like(q, float("nan"))
+            two = torch.full_like(q, float("nan"))
+            E.decode_attention(caches, q, nq, one)
+            E.separate_merge(True)
+            try:
+                E.decode_attention(caches, q, nq, two)
+            finally:
+                E.separate_merge(False)
+            caches[0].synchronize()
+            assert torch.equal(one.view(torch.int32), two.view(torch.int32)), f"call {call}"
+            assert not torch.isnan(one).any()
+    finally:
+        E.force_splits(0)
+    assert E.device_status(0) == 0
+    for c in caches:
+        c.free()

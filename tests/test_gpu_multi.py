@@ -1,0 +1,126 @@
+"""GPU, 2 and 4 ranks: the library's sequence-split decode over NCCL
+(eakv_decode_attention_split, include/eakv_nccl.h), one process per GPU.
+
+Every rank holds its page-aligned slice of the positions of every sequence
+in its own caches; the library decodes the slice, all-gathers the (output,
+LSE) records over its own NCCL communicator and merges them. Each rank's
+result is checked against the oracle's two-pass attention over the whole
+sequence (1e-4 abs + 1e-4 rel), and all ranks must hold the same bits. With
+4 GPUs the KV heads are also split in two head shards, each a sequence-split
+group of 2. Skipped when fewer GPUs than ranks are visible. torch.distributed
+(gloo) only carries the NCCL id; NVLS is off in the children."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from conftest import HAS_GPU
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, hs, lens, result_q):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    dec = None
+    caches = []
+    try:
+        import eakv_b200 as E
+        from eakv_b200.parallel import SeqSplitDecoder, seq_shard
+        from gpu_util import assert_close, kv_data
+        from oracle import oracle as O
+        torch.cuda.set_device(rank)
+        E.set_device(rank)
+        dev = torch.device("cuda", rank)
+        L, nq, nkv, hd = 2, 16, 4, 128
+        ss = world // hs
+        h_i, s_i = rank // ss, rank % ss
+        groups = [dist.new_group(ranks=[h * ss + k for k in range(ss)]) for h in range(hs)]
+        rng = np.random.default_rng(11)              # the same data on every rank
+        datas = [kv_data(rng, L, nkv, n, hd) for n in lens]
+        q = rng.standard_normal((len(lens), L, nq, hd)).astype(np.float32)
+        kh, qh = nkv // hs, nq // hs
+        for b, n in enumerate(lens):
+            lo, hi = seq_shard(n, ss, s_i)
+            c = E.Cache(L, kh, hd, max(hi - lo, 1))
+            if hi > lo:
+                mine = np.ascontiguousarray(datas[b][:, :, h_i * kh:(h_i + 1) * kh, lo:hi])
+                assert c.load_raw(mine, hi - lo) == 0
+            caches.append(c)
+        dec = SeqSplitDecoder(caches, qh, hd, group=groups[h_i], device=rank)
+        dq = torch.from_numpy(np.ascontiguousarray(q[:, :, h_i * qh:(h_i + 1) * qh])).to(dev)
+        stream = torch.cuda.Stream(dev)
+        outs = []
+        for _ in range(2):                           # two steps in a row
+            do = torch.full_like(dq, float("nan"))
+            dec.step(dq, do, stream=stream)
+            stream.synchronize()
+            outs.append(do.cpu().numpy())
+        assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+        for b, n in enumerate(lens):
+            rc = O.RefCache(L, nkv, hd, n)
+            rc.load_raw(datas[b], n)
+            for l in range(L):
+                full = rc.fused(q[b, l], l, nq, nkv).reshape(nq, hd)
+                assert_close(outs[0][b, l], full[h_i * qh:(h_i + 1) * qh],
+                             what=f"rank {rank} sequence {b} layer {l}")
+        assert E.device_status(rank) == 0
+        result_q.put((rank, "ok", outs[0].tobytes()))
+    except Exception as e:                           # noqa: BLE001 - reported to the parent
+        result_q.put((rank, f"{type(e).__name__}: {e}", b""))
+    finally:
+        if dec is not None:
+            dec.close()
+        for c in caches:
+            c.free()
+        dist.destroy_process_group()
+
+
+def _run(world, hs, lens):
+    import torch
+    import torch.multiprocessing as mp
+    if not HAS_GPU or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, hs, lens, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in procs:
+        r, msg, out = q.get(timeout=600)
+        results[r] = (msg, out)
+    for p in procs:
+        p.join(timeout=120)
+    for r, (msg, _) in sorted(results.items()):
+        assert msg == "ok", f"rank {r}: {msg}"
+    ss = world // hs
+    for r in range(world):   # the ranks of a group hold the same bits
+        assert results[r][1] == results[(r // ss) * ss][1], f"rank {r} differs from its group"
+
+
+@pytest.mark.parametrize("lens", [[1000, 333], [50, 2048]])
+def test_sequence_split_two_gpus(lens):
+    """[50, 2048]: the second rank's slice of the first sequence is empty."""
+    _run(2, 1, lens)
+
+
+def test_head_shards_times_sequence_split_four_gpus():
+    _run(4, 2, [1500, 700])

@@ -141,3 +141,26 @@ REFTESTS = sorted(glob.glob(os.path.join(os.path.dirname(O.REF_SO), "reftest_*")
 def test_reference_ctests_on_oracle(exe):
     r = subprocess.run([exe], capture_output=True, text=True, timeout=120)
     assert r.returncode == 0, r.stdout + r.stderr
+
+
+@pytest.mark.parametrize("hd", [64, 128])
+def test_single_head_kernels_match_multi_head_rows(hd):
+    """Row a10: the reference's single-head kernels with a group offset
+    (kernels/fused_k_score.ea:9-153, fused_v_sum.ea:7-77 and their _64 forms)
+    restated, against the pinned multi-head restatements: head h of a
+    multi-head block through the single-head form is row h of the multi-head
+    result, bit for bit."""
+    rng = np.random.default_rng(hd)
+    L, H, S, maxS = 1, 3, 77, 90
+    data = rng.standard_normal((L, 2, H, S, hd)).astype(np.float32)
+    rc = O.RefCache(L, H, hd, maxS)
+    rc.load_raw(data, S)
+    q = rng.standard_normal(H * hd).astype(np.float32)
+    multi = rc.scores(q, 0, H, H).reshape(H, S)
+    w = rng.random(H * S).astype(np.float32)
+    vmulti = rc.output(w, 0, H, H).reshape(H, hd)
+    for h in range(H):
+        assert np.array_equal(bits(rc.scores_single(q[h * hd:(h + 1) * hd], 0, h)),
+                              bits(multi[h]))
+        assert np.array_equal(bits(rc.output_single(w[h * S:(h + 1) * S], 0, h)),
+                              bits(vmulti[h]))
