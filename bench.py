@@ -354,6 +354,8 @@ def run_b200(args, cfg, world, rank, local):
         E.force_path(1)
     if args.splits:
         E.force_splits(args.splits)
+    if args.separate_merge:
+        E.separate_merge(True)
     dev = torch.device("cuda", local)
     # this rank's share: its KV heads (with their query heads) and, under a
     # sequence split, its slice of every sequence
@@ -523,10 +525,7 @@ def run_b200(args, cfg, world, rank, local):
                 c.append_step_device(new_kv, 1)
                 c.advance(1)
         if split:
-            qd.copy_(qh_t, non_blocking=True)
-            step(qd, out)
-            oh_t.copy_(out, non_blocking=True)
-            stream.synchronize()
+            decoder.step_host(qh, oh, stream=sh)
         else:
             E.decode_attention_host(caches, qh, nq, oh, stream=sh)
 
@@ -593,7 +592,8 @@ def run_b200(args, cfg, world, rank, local):
                     "h2d_bytes_per_step": int(qh.nbytes) + (int(kv_host.numel()) * 4
                                                             if appending else 0),
                     "d2h_bytes_per_step": int(oh.nbytes),
-                    "api": "eakv_decode_attention_host"},
+                    "api": ("eakv_decode_attention_split_host" if split
+                            else "eakv_decode_attention_host")},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": f"{peak_kind} hbm_gbs",
                          "traffic": (traffic_ratio * alg_bytes_launch) if traffic_ratio
@@ -977,6 +977,9 @@ def main():
     ap.add_argument("--graph", default="auto", choices=["auto", "on", "off"],
                     help="replay the device step from CUDA graphs (auto: for the small, "
                          "launch-latency-bound configs that flush L2 between steps)")
+    ap.add_argument("--separate-merge", action="store_true",
+                    help="merge sequence splits in a second kernel after the decode instead of "
+                         "in the decode kernel (for side-by-side measurement)")
     ap.add_argument("--splits", type=int, default=0,
                     help="force this many sequence splits per row (0: planner's choice)")
     args = ap.parse_args()

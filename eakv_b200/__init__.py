@@ -93,6 +93,7 @@ SIGNATURES = {
     "eakv_nccl_comm_destroy": (_I, [_P]),
     "eakv_nccl_comm_abort": (_I, [_P]),
     "eakv_decode_attention_split": (_I, [_P, _I, _P, _I, _I, _I, _P, _P, _P]),
+    "eakv_decode_attention_split_host": (_I, [_P, _I, _P, _I, _P, _P, _P]),
     # eakv_ggml.h
     "eakv_quantize_row": (None, [_P, _P, _c.c_int64]),
     "eakv_dequantize_row": (None, [_P, _P, _c.c_int64]),
@@ -435,6 +436,15 @@ def decode_attention_split(caches, d_queries, n_q_heads, d_output, comm, pos_beg
                                                     pos_begin, pos_end, _ptr(d_output), comm.h,
                                                     stream),
                   "eakv_decode_attention_split")
+
+
+def decode_attention_split_host(caches, queries, n_q_heads, output, comm, stream=None):
+    """eakv_decode_attention_split_host: host queries in, merged host output
+    out, copies overlapped with the chunks' split steps."""
+    arr = _handles(caches)
+    return _check(lib().eakv_decode_attention_split_host(arr, len(caches), _ptr(queries),
+                                                         n_q_heads, _ptr(output), comm.h, stream),
+                  "eakv_decode_attention_split_host")
 
 
 def decode_launches(caches, n_q_heads):

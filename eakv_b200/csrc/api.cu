@@ -101,56 +101,15 @@ void fill_batch(DecodeBatch &b, const eakv_cache_t *const *caches, int n) {
   }
 }
 
-}  // namespace eakv
-
-using namespace eakv;
-
-namespace {
-
-// Status word of the current device into a.status; EAKV_ERR_INVALID when its
-// address cannot be looked up (the kernels would have nowhere to report).
-int attach_status(DecodeArgs &a, const char *who) {
-  if (!a.status) {
-    set_error(EAKV_ERR_INVALID, "%s: device status word unavailable", who);
-    return EAKV_ERR_INVALID;
-  }
-  return EAKV_OK;
-}
-
-// Runs the decode with its split counters and workspace from the first
-// cache's scratch, the workspace placed after `reserve` bytes the caller
-// already uses there.
-int run_decode(const eakv_cache_t *c0, DecodeArgs &a, const DecodeBatch &b, size_t reserve,
-               cudaStream_t s, const char *who) {
-  int rc = attach_status(a, who);
-  if (rc) return rc;
-  const size_t ws = decode_workspace_bytes(a, b);
-  const size_t nc = decode_counters(a, b);
-  void *w = nullptr;
-  if (ws || nc) {
-    void *base = nullptr;
-    rc = cache_workspace(c0, nc, reserve + ws, &a.cnt, &base);
-    if (rc) return rc;
-    w = (uint8_t *)base + reserve;
-  }
-  return decode_launch(a, b, ws ? w : nullptr, ws, s);
-}
-
 // ---- pipelined host-buffer decode -------------------------------------------
 
-// Below this many bytes of queries the host-buffer decode is one copy in, one
-// decode and one copy out on the caller's stream.
-constexpr size_t kPipelineMinBytes = 1u << 20;
 
 // Helper streams of the host-buffer decode on one device: queries in,
 // outputs out, and a second compute stream, so that the next chunk's CTAs
 // fill the SMs while the previous chunk's last CTAs drain. Created on first
 // use, kept for the life of the process.
-struct HostStreams {
-  cudaStream_t in = nullptr, out = nullptr, alt = nullptr;
-};
-std::mutex g_host_streams_mu;
-HostStreams g_host_streams[64];
+static std::mutex g_host_streams_mu;
+static HostStreams g_host_streams[64];
 
 int host_streams(int dev, HostStreams &hs) {
   std::lock_guard<std::mutex> lock(g_host_streams_mu);
@@ -197,6 +156,41 @@ int host_chunks(int n, int (&start)[5]) {
   start[3] = n - 1;
   start[4] = n;
   return 4;
+}
+
+}  // namespace eakv
+
+using namespace eakv;
+
+namespace {
+
+// Status word of the current device into a.status; EAKV_ERR_INVALID when its
+// address cannot be looked up (the kernels would have nowhere to report).
+int attach_status(DecodeArgs &a, const char *who) {
+  if (!a.status) {
+    set_error(EAKV_ERR_INVALID, "%s: device status word unavailable", who);
+    return EAKV_ERR_INVALID;
+  }
+  return EAKV_OK;
+}
+
+// Runs the decode with its split counters and workspace from the first
+// cache's scratch, the workspace placed after `reserve` bytes the caller
+// already uses there.
+int run_decode(const eakv_cache_t *c0, DecodeArgs &a, const DecodeBatch &b, size_t reserve,
+               cudaStream_t s, const char *who) {
+  int rc = attach_status(a, who);
+  if (rc) return rc;
+  const size_t ws = decode_workspace_bytes(a, b);
+  const size_t nc = decode_counters(a, b);
+  void *w = nullptr;
+  if (ws || nc) {
+    void *base = nullptr;
+    rc = cache_workspace(c0, nc, reserve + ws, &a.cnt, &base);
+    if (rc) return rc;
+    w = (uint8_t *)base + reserve;
+  }
+  return decode_launch(a, b, ws ? w : nullptr, ws, s);
 }
 
 // The host-buffer decode in chunks of caches (or of layers, for a single

@@ -19,131 +19,320 @@
 #include <math.h>
 #include <stdio.h>
 
+#include <atomic>
+
 #include "internal.cuh"
+#include "pipeline.cuh"
 
 namespace eakv {
 namespace {
 
-constexpr int kScoreThreads = 256;   // 16 positions x 16 lanes
+constexpr int kScoreThreads = 256;   // 8 warps x 8 quads, each quad 2 positions
 constexpr int kHeadChunk = 32;       // query heads per pass (shared memory bound)
 
-// grid: (pages of the sequence, n_kv, head chunks); one page per block.
-__global__ void __launch_bounds__(kScoreThreads)
+// The reference's f32x16 vector of one position's chain, split over a quad of
+// threads: thread t of the quad plays SIMD lanes t, t+4, t+8 and t+12, so the
+// first two levels of the halving-tree reduce_add (lanes l + l+8, then l +
+// l+4) stay inside the thread and only the last two (l + l+2, l + l+1) cross
+// threads. Lane l of group g, step jj runs
+//   acc_l = fma(fma(n, s, b), q[64 g + 16 jj + l], acc_l)
+// over (g, jj) in order: jj = 0, 1 take the low nibbles of bytes l and 16 + l,
+// jj = 2, 3 their high nibbles (kernels/fused_k_score.ea:41-100). Lanes (t,
+// t+4) and (t+8, t+12) run as f32x2 pairs: two independent chains per
+// instruction, each rounded as one fma.
+
+// Bytes t, t+4, t+8, t+12 of a 16-byte chunk (byte t of each of its words).
+__device__ __forceinline__ uint32_t gather_lane_bytes(uint4 v, uint32_t sel) {
+  const uint32_t x = __byte_perm(v.x, v.y, sel);
+  const uint32_t y = __byte_perm(v.z, v.w, sel);
+  return __byte_perm(x, y, 0x5410);
+}
+
+// The four nibbles (one per byte) of w as two exact float pairs, dequantized
+// with one rounding each: (fma(n0, s, b), fma(n1, s, b)), (fma(n2, ...), ...).
+__device__ __forceinline__ void dequant4(uint32_t w, float2 s2, float2 b2, float2 &lo,
+                                         float2 &hi) {
+  const float2 off = make_float2(-8388608.0f, -8388608.0f);
+  const float2 n01 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440)),
+                                            __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7441))),
+                                off);
+  const float2 n23 = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7442)),
+                                            __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7443))),
+                                off);
+  lo = __ffma2_rn(n01, s2, b2);
+  hi = __ffma2_rn(n23, s2, b2);
+}
+
+constexpr int kScorePages = 8;   // pages a block stages at once (40 KB at head_dim 128)
+
+// grid: (page blocks of up to kScorePages pages, n_kv, head chunks). The
+// block's pages arrive in shared memory by one bulk copy each (one mbarrier,
+// bounded wait) while the queries of the chunk are staged; each quad then
+// scores positions p and p + 64 of every 128-position step, for every query
+// head of the chunk, from one dequantization of each K row.
+template <int HD>
+__global__ void __launch_bounds__(kScoreThreads, 2)
 scores_kernel(const uint8_t *__restrict__ buf, PageGeom g, int layer,
-              const float *__restrict__ q, int q_per_kv, int head_dim, int seq_len,
-              float rsqrt_d, float *__restrict__ scores) {
-  extern __shared__ float smem[];
+              const float *__restrict__ q, int q_per_kv, int seq_len, float rsqrt_d,
+              float *__restrict__ scores, int pages_per_block, int *status) {
+  constexpr int GPD = HD / 64;
+  constexpr int PB = kPagePositions * GPD * 40, NIB = kPagePositions * GPD * 32;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t *bar = reinterpret_cast<uint64_t *>(smem);
+  uint8_t *pages = smem + 128;
+  float4 *q_s = reinterpret_cast<float4 *>(pages + kScorePages * PB);   // [nh][GPD][jj][t]
   const int kvh = blockIdx.y;
   const int h0 = blockIdx.z * kHeadChunk;
   const int nh = min(kHeadChunk, q_per_kv - h0);
-  float *q_s = smem;                          // [nh][head_dim]
-  float *sc_s = smem + kHeadChunk * head_dim; // [nh][64]
-  const int page = blockIdx.x;
-  const int l = threadIdx.x & 15;
-  const int slot = threadIdx.x >> 4;          // position slot 0..15
-
-  for (int i = threadIdx.x; i < nh * head_dim; i += blockDim.x) {
-    int j = i / head_dim, d = i - j * head_dim;
-    q_s[i] = q[(size_t)(kvh * q_per_kv + h0 + j) * head_dim + d];
+  const int n_seq_pages = (seq_len + kPagePositions - 1) / kPagePositions;
+  const int pg0 = blockIdx.x * pages_per_block;
+  const int npg = min(n_seq_pages, pg0 + pages_per_block) - pg0;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(bar), 1);
+    fence_mbar_init();
   }
   __syncthreads();
-
-  const uint8_t *pp = buf + page_index(g, layer, 0, kvh, page) * g.page_bytes;
-  const float2 *sb = reinterpret_cast<const float2 *>(pp + g.nib_bytes);
-  for (int sub = 0; sub < 4; sub++) {
-    const int pip = sub * 16 + slot;
-    const int t = page * kPagePositions + pip;
-    const bool valid = t < seq_len;
-    float k[8];   // dequantized elements of this lane, gpd <= 2
-    const int gpd = g.gpd;
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(smem_u32(bar), (uint32_t)(npg * PB));
+    for (int i = 0; i < npg; i++)
+      bulk_g2s(smem_u32(pages + i * PB), buf + page_index(g, layer, 0, kvh, pg0 + i) * g.page_bytes,
+               PB, smem_u32(bar));
+  }
+  for (int i = threadIdx.x; i < nh * HD; i += blockDim.x) {
+    const int j = i / HD, e = i - j * HD;
+    const int grp = e >> 6, jj = (e >> 4) & 3, l = e & 15;
+    reinterpret_cast<float *>(q_s)[(((j * GPD + grp) * 4 + jj) * 4 + (l & 3)) * 4 + (l >> 2)] =
+        q[(size_t)(kvh * q_per_kv + h0 + j) * HD + e];
+  }
+  const bool ok = mbar_wait(smem_u32(bar), 0, kWaitBudget);
+  if (!__syncthreads_and(ok)) {
+    if (threadIdx.x == 0) {
+      if (status) atomicOr(status, kStatusWaitTimeout);
+      mbar_wait(smem_u32(bar), 0, kWaitBudget);   // no copy may outlive the block
+    }
+    return;
+  }
+  const int t = threadIdx.x & 3, quad = threadIdx.x >> 2;
+  const uint32_t sel = (uint32_t)t | ((uint32_t)(4 + t) << 4);
+  const int pos_end = npg * kPagePositions;   // block-local
+  for (int pos0 = 0; pos0 < pos_end; pos0 += 2 * kPagePositions) {
+    float2 k[2][GPD][4][2];   // [position][group][jj][lanes (t, t+4) | (t+8, t+12)]
+    int tp[2];
 #pragma unroll
-    for (int grp = 0; grp < 2; grp++) {
-      if (grp < gpd) {
-        uint32_t b0 = 0, b1 = 0;
-        float2 s = make_float2(0.f, 0.f);
-        if (valid) {
-          const uint8_t *row = pp + (size_t)(pip * gpd + grp) * 32;
-          b0 = row[l];
-          b1 = row[16 + l];
-          s = sb[pip * gpd + grp];
-        }
-        k[4 * grp + 0] = __fmaf_rn((float)(b0 & 15), s.x, s.y);
-        k[4 * grp + 1] = __fmaf_rn((float)(b1 & 15), s.x, s.y);
-        k[4 * grp + 2] = __fmaf_rn((float)(b0 >> 4), s.x, s.y);
-        k[4 * grp + 3] = __fmaf_rn((float)(b1 >> 4), s.x, s.y);
+    for (int p = 0; p < 2; p++) {
+      tp[p] = pos0 + p * kPagePositions + quad;
+      // a block's last step may hold one page only: read the first one again
+      const int pos = tp[p] < pos_end ? tp[p] : pos0 + quad;
+      const uint8_t *pp = pages + (pos / kPagePositions) * PB;
+      const int pip = pos % kPagePositions;
+      const uint4 *row = reinterpret_cast<const uint4 *>(pp + pip * (HD / 2));
+      const float *sb = reinterpret_cast<const float *>(pp + NIB) + pip * GPD * 2;
+#pragma unroll
+      for (int grp = 0; grp < GPD; grp++) {
+        const uint32_t z0 = gather_lane_bytes(row[2 * grp], sel);       // bytes l
+        const uint32_t z1 = gather_lane_bytes(row[2 * grp + 1], sel);   // bytes 16 + l
+        const float2 s2 = make_float2(sb[2 * grp], sb[2 * grp]);
+        const float2 b2 = make_float2(sb[2 * grp + 1], sb[2 * grp + 1]);
+        dequant4(z0 & 0x0F0F0F0Fu, s2, b2, k[p][grp][0][0], k[p][grp][0][1]);
+        dequant4(z1 & 0x0F0F0F0Fu, s2, b2, k[p][grp][1][0], k[p][grp][1][1]);
+        dequant4((z0 >> 4) & 0x0F0F0F0Fu, s2, b2, k[p][grp][2][0], k[p][grp][2][1]);
+        dequant4((z1 >> 4) & 0x0F0F0F0Fu, s2, b2, k[p][grp][3][0], k[p][grp][3][1]);
       }
     }
     for (int j = 0; j < nh; j++) {
-      const float *qj = q_s + j * head_dim;
-      float acc = 0.0f;
+      float2 acc[2][2];
 #pragma unroll
-      for (int grp = 0; grp < 2; grp++) {
-        if (grp < gpd) {
+      for (int p = 0; p < 2; p++) acc[p][0] = acc[p][1] = make_float2(0.0f, 0.0f);
 #pragma unroll
-          for (int jj = 0; jj < 4; jj++)
-            acc = __fmaf_rn(k[4 * grp + jj], qj[grp * 64 + jj * 16 + l], acc);
+      for (int grp = 0; grp < GPD; grp++)
+#pragma unroll
+        for (int jj = 0; jj < 4; jj++) {
+          const float4 qv = q_s[((j * GPD + grp) * 4 + jj) * 4 + t];
+          const float2 qa = make_float2(qv.x, qv.y), qb = make_float2(qv.z, qv.w);
+#pragma unroll
+          for (int p = 0; p < 2; p++) {
+            acc[p][0] = __ffma2_rn(k[p][grp][jj][0], qa, acc[p][0]);
+            acc[p][1] = __ffma2_rn(k[p][grp][jj][1], qb, acc[p][1]);
+          }
         }
+#pragma unroll
+      for (int p = 0; p < 2; p++) {
+        const float2 t1 = __fadd2_rn(acc[p][0], acc[p][1]);   // lanes l + l+8
+        float r = __fadd_rn(t1.x, t1.y);                       // l + l+4
+        r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 2));  // l + l+2
+        r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 1));  // l + l+1
+        const int gpos = pg0 * kPagePositions + tp[p];
+        if (t == 0 && tp[p] < pos_end && gpos < seq_len)
+          scores[(size_t)(kvh * q_per_kv + h0 + j) * seq_len + gpos] = __fmul_rn(r, rsqrt_d);
       }
-      acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 8));
-      acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 4));
-      acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 2));
-      acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, 1));
-      if (l == 0) sc_s[j * 64 + pip] = __fmul_rn(acc, rsqrt_d);
     }
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < nh * 64; i += blockDim.x) {
-    int j = i >> 6, pip = i & 63;
-    int t = page * kPagePositions + pip;
-    if (t < seq_len) scores[(size_t)(kvh * q_per_kv + h0 + j) * seq_len + t] = sc_s[i];
   }
 }
 
-constexpr int kVHeads = 8;   // accumulators per thread
+template <int HD>
+size_t scores_smem() {
+  return 128 + (size_t)kScorePages * kPagePositions * (HD / 64) * 40 +
+         (size_t)kHeadChunk * HD * sizeof(float);
+}
 
-// grid: (chunks, n_kv, head chunks of kVHeads); blockDim = head_dim.
-// Writes d_out directly when there is one chunk, else per-chunk partials.
-__global__ void vsum_kernel(const uint8_t *__restrict__ buf, PageGeom g, int layer,
-                            const float *__restrict__ w, int q_per_kv, int head_dim,
-                            int seq_len, int chunk, float *__restrict__ out,
-                            float *__restrict__ part, int n_q) {
-  extern __shared__ float w_s[];   // [kVHeads][chunk]
+template <int HD>
+cudaError_t launch_scores_hd(dim3 grid, const PageGeom &g, const uint8_t *d_buf, int layer,
+                             const float *d_q, int q_per_kv, int seq_len, float rsqrt_d,
+                             float *d_scores, int ppb, int *status, cudaStream_t s) {
+  static std::atomic<unsigned long long> attr_done{0};   // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_done.load(std::memory_order_acquire) >> (dev & 63) & 1)) {
+    cudaError_t e = cudaFuncSetAttribute(scores_kernel<HD>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)scores_smem<HD>());
+    if (e != cudaSuccess) return e;
+    attr_done.fetch_or(1ull << (dev & 63), std::memory_order_acq_rel);
+  }
+  scores_kernel<HD><<<grid, kScoreThreads, scores_smem<HD>(), s>>>(
+      d_buf, g, layer, d_q, q_per_kv, seq_len, rsqrt_d, d_scores, ppb, status);
+  return cudaGetLastError();
+}
+
+constexpr int kVHeads = 8;          // query heads per block (accumulators per thread)
+constexpr int kVThreads = 128;
+constexpr int kVChunkPages = 16;    // positions of one block: 1024
+constexpr int kVExactMax = 512;     // up to this length the whole sum is one chain
+
+// V sum. Every output element (query head h, dim d) is its own chain over
+// positions, o = fma(fma(n, s, b), w[h][t], o), in position order
+// (kernels/fused_v_sum.ea:111-150). A block takes up to 16 pages of one KV
+// head and up to 8 query heads: one bulk copy per page brings the pages into
+// shared memory (one mbarrier, bounded wait), the weights are staged beside
+// them, and the positions are cut among position streams of HD/8 threads.
+// Thread i of a stream owns bytes 4i..4i+3 of a position's nibble row, i.e.
+// dims b..b+3 and b+32..b+35 of its group, and runs its chains as f32x2
+// pairs. Up to kVExactMax positions a single stream runs the whole sequence
+// (one chain per element, bit-identical to the reference); longer sequences
+// add the streams' sums, then the blocks' sums, in position order, which
+// re-associates the sum (within the 1e-4 bar).
+//
+// grid: (chunks of kVChunkPages pages, n_kv, head groups of kVHeads).
+// Writes d_out directly when there is one chunk, else a partial per chunk.
+template <int HD>
+__global__ void __launch_bounds__(kVThreads)
+vsum_kernel(const uint8_t *__restrict__ buf, PageGeom g, int layer,
+            const float *__restrict__ w, int q_per_kv, int seq_len, int n_chunks,
+            float *__restrict__ out, float *__restrict__ part, int n_q, int *status) {
+  constexpr int GPD = HD / 64, TPS = HD / 8, NSTREAM = kVThreads / TPS;
+  constexpr int PB = kPagePositions * GPD * 40, NIB = kPagePositions * GPD * 32;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t *bar = reinterpret_cast<uint64_t *>(smem);
+  uint8_t *pages = smem + 128;
+  float *w_s = reinterpret_cast<float *>(pages + kVChunkPages * PB);   // [kVHeads][1024]
   const int kvh = blockIdx.y;
   const int h0 = blockIdx.z * kVHeads;
   const int nh = min(kVHeads, q_per_kv - h0);
-  const int t0 = blockIdx.x * chunk;
-  const int t1 = min(seq_len, t0 + chunk);
-  const int n = t1 - t0;
-  for (int i = threadIdx.x; i < nh * chunk; i += blockDim.x) {
-    int j = i / chunk, tt = i - j * chunk;
-    w_s[i] = tt < n ? w[(size_t)(kvh * q_per_kv + h0 + j) * seq_len + t0 + tt] : 0.0f;
+  const int c0 = blockIdx.x * kVChunkPages * kPagePositions;
+  const int len = min(seq_len - c0, kVChunkPages * kPagePositions);
+  const int pg0 = c0 / kPagePositions, npg = (len + kPagePositions - 1) / kPagePositions;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(bar), 1);
+    fence_mbar_init();
   }
   __syncthreads();
-  const int d = threadIdx.x;
-  const int grp = d >> 6, e = d & 63;
-  const int byte = e & 31, shift = (e >> 5) * 4;
-  float o[kVHeads];
-#pragma unroll
-  for (int j = 0; j < kVHeads; j++) o[j] = 0.0f;
-  for (int tt = 0; tt < n; tt++) {
-    const int t = t0 + tt;
-    const int page = t / kPagePositions, pip = t - page * kPagePositions;
-    const uint8_t *pp = buf + page_index(g, layer, 1, kvh, page) * g.page_bytes;
-    const int slot = pip * g.gpd + grp;
-    const float nib = (float)((pp[(size_t)slot * 32 + byte] >> shift) & 15);
-    const float2 s = reinterpret_cast<const float2 *>(pp + g.nib_bytes)[slot];
-    const float v = __fmaf_rn(nib, s.x, s.y);
-#pragma unroll
-    for (int j = 0; j < kVHeads; j++)
-      if (j < nh) o[j] = __fmaf_rn(v, w_s[j * chunk + tt], o[j]);
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(smem_u32(bar), (uint32_t)(npg * PB));
+    for (int i = 0; i < npg; i++)
+      bulk_g2s(smem_u32(pages + i * PB),
+               buf + page_index(g, layer, 1, kvh, pg0 + i) * g.page_bytes, PB, smem_u32(bar));
   }
-  float *dst = gridDim.x == 1 ? out : part + (size_t)blockIdx.x * n_q * head_dim;
-  for (int j = 0; j < nh; j++) dst[(size_t)(kvh * q_per_kv + h0 + j) * head_dim + d] = o[j];
+  // weights of the chunk, eight loads in flight per thread before any store
+  for (int i0 = 0; i0 < nh * len; i0 += 8 * kVThreads) {
+    float wv[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int i = i0 + u * kVThreads + threadIdx.x;
+      const int j = i / len, tt = i - j * len;
+      wv[u] = i < nh * len ? __ldg(w + (size_t)(kvh * q_per_kv + h0 + j) * seq_len + c0 + tt)
+                           : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int i = i0 + u * kVThreads + threadIdx.x;
+      const int j = i / len, tt = i - j * len;
+      if (i < nh * len) w_s[j * kVChunkPages * kPagePositions + tt] = wv[u];
+    }
+  }
+  const bool ok = mbar_wait(smem_u32(bar), 0, kWaitBudget);
+  if (!__syncthreads_and(ok)) {
+    if (threadIdx.x == 0) {
+      if (status) atomicOr(status, kStatusWaitTimeout);
+      mbar_wait(smem_u32(bar), 0, kWaitBudget);   // no copy may outlive the block
+    }
+    return;
+  }
+  const int stream = threadIdx.x / TPS, i = threadIdx.x - stream * TPS;
+  const int nused = seq_len <= kVExactMax ? 1 : NSTREAM;
+  const int sub = (len + nused - 1) / nused;
+  const int t0 = stream * sub, t1 = min(len, t0 + sub);
+  const int grp = (4 * i) / 32;
+  float2 o[kVHeads][4];
+#pragma unroll
+  for (int j = 0; j < kVHeads; j++)
+#pragma unroll
+    for (int k = 0; k < 4; k++) o[j][k] = make_float2(0.0f, 0.0f);
+  if (stream < nused) {
+#pragma unroll 4
+    for (int tt = t0; tt < t1; tt++) {
+      const uint8_t *pp = pages + (tt / kPagePositions) * PB;
+      const int pip = tt % kPagePositions;
+      const uint32_t word = *reinterpret_cast<const uint32_t *>(pp + pip * (HD / 2) + 4 * i);
+      const float2 sb = *reinterpret_cast<const float2 *>(pp + NIB + (pip * GPD + grp) * 8);
+      const float2 s2 = make_float2(sb.x, sb.x), b2 = make_float2(sb.y, sb.y);
+      float2 v[4];
+      dequant4(word & 0x0F0F0F0Fu, s2, b2, v[0], v[1]);
+      dequant4((word >> 4) & 0x0F0F0F0Fu, s2, b2, v[2], v[3]);
+#pragma unroll
+      for (int j = 0; j < kVHeads; j++) {
+        if (j < nh) {
+          const float wj = w_s[j * kVChunkPages * kPagePositions + tt];
+          const float2 w2 = make_float2(wj, wj);
+#pragma unroll
+          for (int k = 0; k < 4; k++) o[j][k] = __ffma2_rn(v[k], w2, o[j][k]);
+        }
+      }
+    }
+  }
+  // element (j, dim) of this thread: dims b..b+3 (v[0], v[1]) and b+32..b+35
+  const int dim0 = grp * 64 + (4 * i) % 32;
+  float *dst = n_chunks == 1 ? out : part + (size_t)blockIdx.x * n_q * HD;
+  if (nused == 1) {
+    if (stream == 0) {
+      for (int j = 0; j < nh; j++) {
+        float *r = dst + (size_t)(kvh * q_per_kv + h0 + j) * HD + dim0;
+        *reinterpret_cast<float4 *>(r) = make_float4(o[j][0].x, o[j][0].y, o[j][1].x, o[j][1].y);
+        *reinterpret_cast<float4 *>(r + 32) =
+            make_float4(o[j][2].x, o[j][2].y, o[j][3].x, o[j][3].y);
+      }
+    }
+    return;
+  }
+  // add the streams' sums in position order, through shared memory
+  __syncthreads();   // the pages are no longer read
+  float *acc_s = reinterpret_cast<float *>(pages);   // [NSTREAM][kVHeads][HD]
+  for (int j = 0; j < nh; j++) {
+    float *r = acc_s + (stream * kVHeads + j) * HD + dim0;
+    *reinterpret_cast<float4 *>(r) = make_float4(o[j][0].x, o[j][0].y, o[j][1].x, o[j][1].y);
+    *reinterpret_cast<float4 *>(r + 32) = make_float4(o[j][2].x, o[j][2].y, o[j][3].x, o[j][3].y);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < nh * HD; e += kVThreads) {
+    const int j = e / HD, d = e - j * HD;
+    float a = acc_s[j * HD + d];
+    for (int st = 1; st < NSTREAM; st++) a = __fadd_rn(a, acc_s[(st * kVHeads + j) * HD + d]);
+    dst[(size_t)(kvh * q_per_kv + h0 + j) * HD + d] = a;
+  }
 }
 
 // out[i] = part[0][i] + part[1][i] + ... in chunk order.
 __global__ void vsum_combine_kernel(const float *__restrict__ part, int n_chunks, size_t n,
-                                    float *__restrict__ out) {
+                                   float *__restrict__ out) {
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x) {
     float acc = part[i];
@@ -158,16 +347,34 @@ __global__ void fill_kernel(float *p, size_t n, float v) {
     p[i] = v;
 }
 
-int vsum_chunk(int seq_len, int n_kv) {
-  // Whole sequence in one chunk while it is short (bit-exact with the
-  // reference); otherwise enough chunks for ~2 blocks per SM.
-  if (seq_len <= 512) return seq_len > 0 ? seq_len : 1;
-  int want_chunks = (2 * 148 + n_kv - 1) / n_kv;
-  int c = (seq_len + want_chunks - 1) / want_chunks;
-  c = (c + 63) / 64 * 64;
-  if (c < 256) c = 256;
-  if (c > 2048) c = 2048;
-  return c;
+int vsum_chunks(int seq_len) {
+  const int per = kVChunkPages * kPagePositions;
+  return seq_len > 0 ? (seq_len + per - 1) / per : 1;
+}
+
+template <int HD>
+size_t vsum_smem() {
+  return 128 + (size_t)kVChunkPages * kPagePositions * (HD / 64) * 40 +
+         (size_t)kVHeads * kVChunkPages * kPagePositions * sizeof(float);
+}
+
+template <int HD>
+cudaError_t launch_vsum_hd(dim3 grid, const PageGeom &g, const uint8_t *d_buf, int layer,
+                           const float *d_w, int q_per_kv, int seq_len, int n_chunks, float *d_out,
+                           float *d_part, int n_q, int *status, cudaStream_t s) {
+  static std::atomic<unsigned long long> attr_done{0};   // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_done.load(std::memory_order_acquire) >> (dev & 63) & 1)) {
+    cudaError_t e = cudaFuncSetAttribute(vsum_kernel<HD>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)vsum_smem<HD>());
+    if (e != cudaSuccess) return e;
+    attr_done.fetch_or(1ull << (dev & 63), std::memory_order_acq_rel);
+  }
+  vsum_kernel<HD><<<grid, kVThreads, vsum_smem<HD>(), s>>>(d_buf, g, layer, d_w, q_per_kv, seq_len,
+                                                           n_chunks, d_out, d_part, n_q, status);
+  return cudaGetLastError();
 }
 
 }  // namespace
@@ -178,16 +385,24 @@ cudaError_t launch_scores(const PageGeom &g, const uint8_t *d_buf, int layer, co
   if (seq_len <= 0) return cudaSuccess;
   const int q_per_kv = n_q / n_kv;
   const int head_dim = g.gpd * 64;
-  dim3 grid((seq_len + 63) / 64, n_kv, (q_per_kv + kHeadChunk - 1) / kHeadChunk);
-  size_t smem = (size_t)kHeadChunk * (head_dim + 64) * sizeof(float);
-  scores_kernel<<<grid, kScoreThreads, smem, s>>>(d_buf, g, layer, d_q, q_per_kv, head_dim,
-                                                  seq_len, rsqrt_d, d_scores);
-  return cudaGetLastError();
+  const int pages = (seq_len + 63) / 64;
+  const int chunks = (q_per_kv + kHeadChunk - 1) / kHeadChunk;
+  // about four blocks per SM in all, each a whole number of 128-position
+  // steps and at most kScorePages pages
+  int ppb = (int)(((long long)pages * n_kv * chunks + 591) / 592);
+  ppb = ppb < 2 ? 2 : (ppb + 1) / 2 * 2;
+  if (ppb > kScorePages) ppb = kScorePages;
+  dim3 grid((pages + ppb - 1) / ppb, n_kv, chunks);
+  int *status = device_status_ptr();
+  return head_dim == 128
+             ? launch_scores_hd<128>(grid, g, d_buf, layer, d_q, q_per_kv, seq_len, rsqrt_d,
+                                     d_scores, ppb, status, s)
+             : launch_scores_hd<64>(grid, g, d_buf, layer, d_q, q_per_kv, seq_len, rsqrt_d,
+                                    d_scores, ppb, status, s);
 }
 
 size_t vsum_scratch_floats(const PageGeom &g, int n_q, int seq_len) {
-  int chunk = vsum_chunk(seq_len, 1);
-  int n_chunks = (seq_len + chunk - 1) / chunk;
+  const int n_chunks = vsum_chunks(seq_len);
   return n_chunks > 1 ? (size_t)n_chunks * n_q * g.gpd * 64 : 0;
 }
 
@@ -200,21 +415,17 @@ cudaError_t launch_vsum(const PageGeom &g, const uint8_t *d_buf, int layer, cons
     return cudaGetLastError();
   }
   const int q_per_kv = n_q / n_kv;
-  int chunk = vsum_chunk(seq_len, n_kv);
-  int n_chunks = (seq_len + chunk - 1) / chunk;
-  if (n_chunks > 1 && (size_t)n_chunks * n_q * head_dim > part_floats) {
-    chunk = seq_len;   // not enough scratch: single chunk
-    n_chunks = 1;
-  }
+  const int n_chunks = vsum_chunks(seq_len);
+  if (n_chunks > 1 && (size_t)n_chunks * n_q * head_dim > part_floats)
+    return cudaErrorInvalidValue;   // the caller sizes the partials with vsum_scratch_floats
   dim3 grid(n_chunks, n_kv, (q_per_kv + kVHeads - 1) / kVHeads);
-  size_t smem = (size_t)kVHeads * chunk * sizeof(float);
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(vsum_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) return e;
-  }
-  vsum_kernel<<<grid, head_dim, smem, s>>>(d_buf, g, layer, d_w, q_per_kv, head_dim, seq_len,
-                                           chunk, d_out, d_part, n_q);
+  int *status = device_status_ptr();
+  cudaError_t e = head_dim == 128
+                      ? launch_vsum_hd<128>(grid, g, d_buf, layer, d_w, q_per_kv, seq_len, n_chunks,
+                                            d_out, d_part, n_q, status, s)
+                      : launch_vsum_hd<64>(grid, g, d_buf, layer, d_w, q_per_kv, seq_len, n_chunks,
+                                           d_out, d_part, n_q, status, s);
+  if (e != cudaSuccess) return e;
   if (n_chunks > 1) {
     size_t n = (size_t)n_q * head_dim;
     vsum_combine_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(d_part, n_chunks, n, d_out);

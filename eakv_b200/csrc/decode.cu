@@ -377,7 +377,9 @@ decode_simt_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
     }
   }
   // the item's last split to finish merges all of them
-  if (a.n_splits > 1 && !a.sep_merge && arrive_last(a)) merge_splits<HD>(a, row0, GC);
+  // (the ring is free again)
+  if (a.n_splits > 1 && !a.sep_merge && arrive_last(a))
+    merge_splits<HD, GC, C::THREADS>(a, row0, GC, reinterpret_cast<float *>(smem));
 }
 
 // Exact merge of partial results given as (normalized output, natural LSE).

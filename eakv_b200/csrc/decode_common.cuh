@@ -100,30 +100,141 @@ __device__ __forceinline__ bool arrive_last(const DecodeArgs &a) {
 }
 
 // Exact log-sum-exp merge of element d of row `row` over its splits (base-2
-// maxima), in split order.
+// maxima), in split order. The records are read four splits at a time with
+// their loads issued together (the sums stay in split order), so a merge
+// waits for about ns / 4 round trips to L2 rather than ns.
 template <int HD>
 __device__ __forceinline__ void merge_row(const DecodeArgs &a, size_t row, int d) {
   const int ns = a.n_splits;
+  const float *pm = a.part_m + row * ns, *pl = a.part_l + row * ns;
+  const float *po = a.part_o + row * ns * HD + d;
   float M = -INFINITY;
-  for (int s = 0; s < ns; s++) M = fmaxf(M, __ldcg(a.part_m + row * ns + s));
+  int s = 0;
+  for (; s + 4 <= ns; s += 4) {
+    const float m0 = __ldcg(pm + s), m1 = __ldcg(pm + s + 1), m2 = __ldcg(pm + s + 2),
+                m3 = __ldcg(pm + s + 3);
+    M = fmaxf(fmaxf(fmaxf(fmaxf(M, m0), m1), m2), m3);
+  }
+  for (; s < ns; s++) M = fmaxf(M, __ldcg(pm + s));
   float O = 0.0f, L = 0.0f;
   if (M != -INFINITY) {
-    for (int s = 0; s < ns; s++) {
-      const float f = ex2(__ldcg(a.part_m + row * ns + s) - M);
-      O = fmaf(f, __ldcg(a.part_o + (row * ns + s) * HD + d), O);
-      L = fmaf(f, __ldcg(a.part_l + row * ns + s), L);
+    s = 0;
+    for (; s + 4 <= ns; s += 4) {
+      float m[4], o[4], l[4];
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        m[k] = __ldcg(pm + s + k);
+        o[k] = __ldcg(po + (size_t)(s + k) * HD);
+        l[k] = __ldcg(pl + s + k);
+      }
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const float f = ex2(m[k] - M);
+        O = fmaf(f, o[k], O);
+        L = fmaf(f, l[k], L);
+      }
+    }
+    for (; s < ns; s++) {
+      const float f = ex2(__ldcg(pm + s) - M);
+      O = fmaf(f, __ldcg(po + (size_t)s * HD), O);
+      L = fmaf(f, __ldcg(pl + s), L);
     }
   }
   a.out[row * HD + d] = O / L;
   if (a.lse && d == 0) a.lse[row] = L > 0.0f ? (M + log2f(L)) * kLn2 : -INFINITY;
 }
 
-// The merge of rows row0 .. row0 + n_rows - 1 by the threads of one CTA.
-template <int HD>
-__device__ __forceinline__ void merge_splits(const DecodeArgs &a, size_t row0, int n_rows) {
-  for (int idx = threadIdx.x; idx < n_rows * HD; idx += blockDim.x) {
-    const int h = idx / HD;
-    merge_row<HD>(a, row0 + h, idx - h * HD);
+constexpr int kMergeSmemSplits = 64;   // split counts the staged merge serves
+
+// The merge of rows row0 .. row0 + n_rows - 1 (n_rows <= NR) by the NT
+// threads of one CTA, with the same arithmetic as merge_row. Up to
+// kMergeSmemSplits splits the row maxima, the split weights ex2(m_s - M) and
+// the sums L are computed once per row into shared memory `ws` (NR *
+// (kMergeSmemSplits + 2) floats, free at this point), and each thread then
+// issues the output-record loads of all its elements, four splits at a time,
+// before it adds them: a few round trips to L2 instead of one per element and
+// split. More splits take merge_row per element.
+template <int HD, int NR, int NT>
+__device__ __forceinline__ void merge_splits(const DecodeArgs &a, size_t row0, int n_rows,
+                                             float *ws) {
+  const int ns = a.n_splits;
+  if (ns > kMergeSmemSplits) {
+    for (int idx = threadIdx.x; idx < n_rows * HD; idx += NT) {
+      const int h = idx / HD;
+      merge_row<HD>(a, row0 + h, idx - h * HD);
+    }
+    return;
+  }
+  float *f_s = ws;                                 // [NR][kMergeSmemSplits]: m, then weights
+  float *M_s = ws + NR * kMergeSmemSplits;         // [NR]
+  float *L_s = M_s + NR;                           // [NR]
+  float *l_s = L_s + NR;                           // [NR][kMergeSmemSplits]
+  for (int idx = threadIdx.x; idx < n_rows * ns; idx += NT) {
+    const int h = idx / ns, sp = idx - h * ns;
+    f_s[h * kMergeSmemSplits + sp] = __ldcg(a.part_m + (row0 + h) * ns + sp);
+    l_s[h * kMergeSmemSplits + sp] = __ldcg(a.part_l + (row0 + h) * ns + sp);
+  }
+  __syncthreads();
+  if (threadIdx.x < n_rows) {
+    const int h = threadIdx.x;
+    float M = -INFINITY;
+    for (int sp = 0; sp < ns; sp++) M = fmaxf(M, f_s[h * kMergeSmemSplits + sp]);
+    float L = 0.0f;
+    if (M != -INFINITY) {
+      for (int sp = 0; sp < ns; sp++) {
+        const float f = ex2(f_s[h * kMergeSmemSplits + sp] - M);
+        f_s[h * kMergeSmemSplits + sp] = f;
+        L = fmaf(f, l_s[h * kMergeSmemSplits + sp], L);
+      }
+    }
+    M_s[h] = M;
+    L_s[h] = L;
+  }
+  __syncthreads();
+  constexpr int EPT = (NR * HD + NT - 1) / NT;   // elements per thread
+  float O[EPT];
+  int hh[EPT], dd[EPT];
+#pragma unroll
+  for (int k = 0; k < EPT; k++) {
+    const int idx = threadIdx.x + k * NT;
+    hh[k] = idx / HD;
+    dd[k] = idx - hh[k] * HD;
+    O[k] = 0.0f;
+  }
+  int sp = 0;
+  for (; sp + 4 <= ns; sp += 4) {
+    float o[EPT][4];
+#pragma unroll
+    for (int k = 0; k < EPT; k++)
+#pragma unroll
+      for (int u = 0; u < 4; u++)
+        o[k][u] = hh[k] < n_rows
+                      ? __ldcg(a.part_o + ((row0 + hh[k]) * ns + sp + u) * HD + dd[k])
+                      : 0.0f;
+#pragma unroll
+    for (int k = 0; k < EPT; k++)
+#pragma unroll
+      for (int u = 0; u < 4; u++)
+        if (hh[k] < n_rows && M_s[hh[k]] != -INFINITY)
+          O[k] = fmaf(f_s[hh[k] * kMergeSmemSplits + sp + u], o[k][u], O[k]);
+  }
+  for (; sp < ns; sp++) {
+    float o[EPT];
+#pragma unroll
+    for (int k = 0; k < EPT; k++)
+      o[k] = hh[k] < n_rows ? __ldcg(a.part_o + ((row0 + hh[k]) * ns + sp) * HD + dd[k]) : 0.0f;
+#pragma unroll
+    for (int k = 0; k < EPT; k++)
+      if (hh[k] < n_rows && M_s[hh[k]] != -INFINITY)
+        O[k] = fmaf(f_s[hh[k] * kMergeSmemSplits + sp], o[k], O[k]);
+  }
+#pragma unroll
+  for (int k = 0; k < EPT; k++) {
+    if (hh[k] >= n_rows) continue;
+    const size_t row = row0 + hh[k];
+    const float L = L_s[hh[k]], M = M_s[hh[k]];
+    a.out[row * HD + dd[k]] = O[k] / L;
+    if (a.lse && dd[k] == 0) a.lse[row] = L > 0.0f ? (M + log2f(L)) * kLn2 : -INFINITY;
   }
 }
 

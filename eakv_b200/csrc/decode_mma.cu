@@ -612,8 +612,9 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
       }
     }
   }
-  // the item's last split to finish merges all of them
-  if (a.n_splits > 1 && !a.sep_merge && arrive_last(a)) merge_splits<HD>(a, row0, gh);
+  // the item's last split to finish merges all of them (the ring is free)
+  if (a.n_splits > 1 && !a.sep_merge && arrive_last(a))
+    merge_splits<HD, RH, C::THREADS>(a, row0, gh, reinterpret_cast<float *>(smem));
 }
 
 template <int HD, int RH>

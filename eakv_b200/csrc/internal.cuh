@@ -194,6 +194,18 @@ int *device_status_ptr();   // status word of the current device
 int check_batch(const eakv_cache_t *const *caches, int n, int n_q, const char *who);
 DecodeArgs base_args(const eakv_cache_t *c0, int n_caches, int n_q);
 void fill_batch(DecodeBatch &b, const eakv_cache_t *const *caches, int n);
+
+// Host-buffer pipelines (api.cu): helper streams per device (queries in,
+// outputs out, a second compute stream), created on first use; and the cut of
+// n units (caches) into up to four chunks whose copies overlap the other
+// chunks' work, a one-unit chunk first and last. Below kPipelineMinBytes of
+// queries a call is not cut.
+struct HostStreams {
+  cudaStream_t in = nullptr, out = nullptr, alt = nullptr;
+};
+constexpr size_t kPipelineMinBytes = 1u << 20;
+int host_streams(int dev, HostStreams &hs);
+int host_chunks(int n, int (&start)[5]);
 // decode_mma.cu: tensor-core decode, any number of query heads per KV head
 int mma_heads_per_cta(int G, int head_dim);   // 0 when the head_dim is not served
 int mma_resident(int gh, int head_dim);

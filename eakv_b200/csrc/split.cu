@@ -104,6 +104,43 @@ size_t record_floats(size_t rows, int head_dim) {
   return (rows * (head_dim + 1) + 63) / 64 * 64;
 }
 
+// Queues one split step of batch (a, b) on stream s: the partial decode into
+// this rank's record slot, the all-gather of the records, the merge into
+// d_out. records holds world * rec floats; ws / ws_bytes are the decode's
+// split workspace (a.cnt its counters).
+int split_launch(const NcclApi *n, ncclComm_t nc, int world, int rank, DecodeArgs a,
+                 const DecodeBatch &b, float *records, size_t rec, void *ws, size_t ws_bytes,
+                 float *d_out, cudaStream_t s) {
+  const size_t rows = (size_t)a.n_caches * a.n_layers * a.n_q_heads;
+  float *mine = records + (size_t)rank * rec;
+  a.out = mine;
+  a.lse = mine + rows * a.head_dim;
+  int rc = decode_launch(a, b, ws, ws_bytes, s);
+  if (rc) return rc;
+  if (world > 1) {
+    rc = check_nccl(n, n->all_gather(mine, records, rec, ncclFloat32, nc, s), "ncclAllGather");
+    if (rc) return rc;
+  }
+  return lse_combine_launch(world, (int)rows, a.head_dim, records, rec, records + rows * a.head_dim,
+                            rec, d_out, nullptr, s);
+}
+
+// The communicator's size, this rank, and a check that it lives on `device`.
+int comm_info(const NcclApi *n, ncclComm_t nc, int device, int &world, int &rank,
+              const char *who) {
+  int cdev = -1;
+  int rc = check_nccl(n, n->comm_count(nc, &world), "ncclCommCount");
+  if (!rc) rc = check_nccl(n, n->comm_user_rank(nc, &rank), "ncclCommUserRank");
+  if (!rc) rc = check_nccl(n, n->comm_cu_device(nc, &cdev), "ncclCommCuDevice");
+  if (rc) return rc;
+  if (cdev != device) {
+    set_error(EAKV_ERR_INVALID, "%s: communicator on device %d, caches on device %d", who, cdev,
+              device);
+    return EAKV_ERR_INVALID;
+  }
+  return EAKV_OK;
+}
+
 }  // namespace
 }  // namespace eakv
 
@@ -183,17 +220,10 @@ int eakv_decode_attention_split(const eakv_cache_t *const *caches, int n_caches,
   const NcclApi *n = nccl(who);
   if (!n) return EAKV_ERR_INVALID;
   ncclComm_t nc = (ncclComm_t)comm;
-  int world = 0, rank = 0, cdev = -1;
-  rc = check_nccl(n, n->comm_count(nc, &world), "ncclCommCount");
-  if (!rc) rc = check_nccl(n, n->comm_user_rank(nc, &rank), "ncclCommUserRank");
-  if (!rc) rc = check_nccl(n, n->comm_cu_device(nc, &cdev), "ncclCommCuDevice");
-  if (rc) return rc;
   const eakv_cache_t *c0 = caches[0];
-  if (cdev != c0->device) {
-    set_error(EAKV_ERR_INVALID, "%s: communicator on device %d, caches on device %d", who, cdev,
-              c0->device);
-    return EAKV_ERR_INVALID;
-  }
+  int world = 0, rank = 0;
+  rc = comm_info(n, nc, c0->device, world, rank, who);
+  if (rc) return rc;
   DeviceGuard g(c0->device);
   cudaStream_t s = stream ? (cudaStream_t)stream : c0->stream;
   DecodeArgs a = base_args(c0, n_caches, n_q);
@@ -206,27 +236,126 @@ int eakv_decode_attention_split(const eakv_cache_t *const *caches, int n_caches,
   a.pos_end = pos_end;
   DecodeBatch b;
   fill_batch(b, caches, n_caches);
-  const int hd = c0->head_dim;
   const size_t rows = (size_t)n_caches * c0->n_layers * n_q;
-  const size_t rec = record_floats(rows, hd);
+  const size_t rec = record_floats(rows, c0->head_dim);
   // scratch: [records of every rank | decode split workspace]
   const size_t rec_bytes = (size_t)world * rec * sizeof(float);
   const size_t ws = decode_workspace_bytes(a, b);
   void *base = nullptr;
   rc = cache_workspace(c0, decode_counters(a, b), rec_bytes + ws, &a.cnt, &base);
   if (rc) return rc;
-  float *records = (float *)base;
-  float *mine = records + (size_t)rank * rec;
-  a.out = mine;
-  a.lse = mine + rows * hd;
-  rc = decode_launch(a, b, ws ? (uint8_t *)base + rec_bytes : nullptr, ws, s);
+  return split_launch(n, nc, world, rank, a, b, (float *)base, rec,
+                      ws ? (uint8_t *)base + rec_bytes : nullptr, ws, d_out, s);
+}
+
+int eakv_decode_attention_split_host(const eakv_cache_t *const *caches, int n_caches,
+                                     const float *queries, int n_q, float *output, void *comm,
+                                     void *stream) {
+  clear_error();
+  const char *who = "decode_attention_split_host";
+  int rc = check_batch(caches, n_caches, n_q, who);
   if (rc) return rc;
-  if (world > 1) {
-    rc = check_nccl(n, n->all_gather(mine, records, rec, ncclFloat32, nc, s), "ncclAllGather");
-    if (rc) return rc;
+  if (!queries || !output || !comm) {
+    set_error(EAKV_ERR_INVALID, "%s: invalid argument", who);
+    return EAKV_ERR_INVALID;
   }
-  return lse_combine_launch(world, (int)rows, hd, records, rec, records + rows * hd, rec, d_out,
-                            nullptr, s);
+  const NcclApi *n = nccl(who);
+  if (!n) return EAKV_ERR_INVALID;
+  ncclComm_t nc = (ncclComm_t)comm;
+  const eakv_cache_t *c0 = caches[0];
+  int world = 0, rank = 0;
+  rc = comm_info(n, nc, c0->device, world, rank, who);
+  if (rc) return rc;
+  DeviceGuard g(c0->device);
+  cudaStream_t s = stream ? (cudaStream_t)stream : c0->stream;
+  HostStreams hs;
+  rc = host_streams(c0->device, hs);
+  if (rc) return rc;
+  DecodeArgs a = base_args(c0, n_caches, n_q);
+  if (!a.status) {
+    set_error(EAKV_ERR_INVALID, "%s: device status word unavailable", who);
+    return EAKV_ERR_INVALID;
+  }
+  DecodeBatch b;
+  fill_batch(b, caches, n_caches);
+  decode_fix_plan(a, b);   // every chunk keeps the whole batch's split plan
+  const int hd = c0->head_dim;
+  const size_t unit = (size_t)c0->n_layers * n_q * hd;   // floats of one cache's queries
+  const size_t nfl = (size_t)n_caches * unit;
+  int start[5];
+  const int nch = n_caches > 1 && nfl * sizeof(float) >= kPipelineMinBytes
+                      ? host_chunks(n_caches, start) : (start[0] = 0, start[1] = n_caches, 1);
+  // the largest chunk sets the records and workspace sizes; the chunks run
+  // one after another on stream s, so they share both
+  DecodeArgs ca[4];
+  DecodeBatch cb[4];
+  size_t rec = 0, ws = 0, cnt = 0;
+  for (int k = 0; k < nch; k++) {
+    const int cn = start[k + 1] - start[k];
+    ca[k] = a;
+    ca[k].n_caches = cn;
+    fill_batch(cb[k], caches + start[k], cn);
+    const size_t r = record_floats((size_t)cn * c0->n_layers * n_q, hd);
+    const size_t w = decode_workspace_bytes(ca[k], cb[k]);
+    const size_t c = decode_counters(ca[k], cb[k]);
+    if (r > rec) rec = r;
+    if (w > ws) ws = w;
+    if (c > cnt) cnt = c;
+  }
+  const size_t half = (nfl * sizeof(float) + 255) / 256 * 256;
+  const size_t rec_bytes = ((size_t)world * rec * sizeof(float) + 255) / 256 * 256;
+  void *vbase = nullptr;
+  unsigned *counters = nullptr;
+  rc = cache_workspace(c0, cnt, 2 * half + rec_bytes + ws, &counters, &vbase);
+  if (rc) return rc;
+  uint8_t *base = (uint8_t *)vbase;
+  float *dq = (float *)base, *dout = (float *)(base + half);
+  float *records = (float *)(base + 2 * half);
+  void *wsp = ws ? base + 2 * half + rec_bytes : nullptr;
+
+  cudaEvent_t ev[9] = {};
+  int made = 0;
+  for (; made < 2 * nch + 1; made++) {
+    rc = check_cuda(cudaEventCreateWithFlags(&ev[made], cudaEventDisableTiming), who);
+    if (rc) break;
+  }
+  cudaEvent_t ev0 = ev[0], *ev_in = ev + 1, *ev_done = ev + 1 + nch;
+  auto step = [&](cudaError_t e) {
+    if (!rc) rc = check_cuda(e, who);
+  };
+  if (!rc) {
+    step(cudaEventRecord(ev0, s));
+    step(cudaStreamWaitEvent(hs.in, ev0, 0));
+    for (int k = 0; k < nch && !rc; k++) {
+      const size_t off = start[k] * unit, len = (start[k + 1] - start[k]) * unit;
+      step(cudaMemcpyAsync(dq + off, queries + off, len * sizeof(float), cudaMemcpyHostToDevice,
+                           hs.in));
+      step(cudaEventRecord(ev_in[k], hs.in));
+    }
+    for (int k = 0; k < nch && !rc; k++) {
+      const size_t off = start[k] * unit;
+      step(cudaStreamWaitEvent(s, ev_in[k], 0));
+      if (rc) break;
+      ca[k].q = dq + off;
+      ca[k].cnt = counters;
+      rc = split_launch(n, nc, world, rank, ca[k], cb[k], records, rec, wsp, ws, dout + off, s);
+      step(cudaEventRecord(ev_done[k], s));
+    }
+    for (int k = 0; k < nch && !rc; k++) {
+      const size_t off = start[k] * unit, len = (start[k + 1] - start[k]) * unit;
+      step(cudaStreamWaitEvent(hs.out, ev_done[k], 0));
+      step(cudaMemcpyAsync(output + off, dout + off, len * sizeof(float), cudaMemcpyDeviceToHost,
+                           hs.out));
+    }
+  }
+  // nothing of this call is left in flight when it returns, error or not
+  const cudaStream_t all[3] = {hs.in, s, hs.out};
+  for (cudaStream_t t : all) {
+    cudaError_t e = cudaStreamSynchronize(t);
+    if (!rc && e != cudaSuccess) rc = check_cuda(e, who);
+  }
+  for (int i = 0; i < made; i++) cudaEventDestroy(ev[i]);
+  return rc;
 }
 
 }  // extern "C"

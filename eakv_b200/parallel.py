@@ -112,5 +112,13 @@ class SeqSplitDecoder:
         decode_attention_split(self.caches, d_q, self.n_q, d_out, self.comm, stream=h)
         return d_out
 
+    def step_host(self, queries, output, stream=None):
+        """One step with host buffers (numpy or pinned torch CPU tensors):
+        copies overlapped with the library's chunked split steps."""
+        from . import decode_attention_split_host
+        h = getattr(stream, "cuda_stream", stream)
+        decode_attention_split_host(self.caches, queries, self.n_q, output, self.comm, stream=h)
+        return output
+
     def close(self):
         self.comm.destroy()

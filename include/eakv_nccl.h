@@ -64,6 +64,17 @@ int eakv_decode_attention_split(const eakv_cache_t *const *caches, int n_caches,
                                 const float *d_queries, int n_q_heads, int pos_begin,
                                 int pos_end, float *d_output, void *comm, void *stream);
 
+/* Same step with host buffers (queries / output f32[n_caches][n_layers]
+ * [n_q_heads][head_dim]): copies in, runs the step, copies out, and returns
+ * when done. From 1 MiB of queries on, the caches are cut into up to four
+ * chunks, each its own split step (its own all-gather) on `stream`, whose
+ * copies overlap the other chunks' steps; every rank must make the same
+ * call, so the chunks and their collectives match. Every chunk keeps the
+ * whole batch's split plan. */
+int eakv_decode_attention_split_host(const eakv_cache_t *const *caches, int n_caches,
+                                     const float *queries, int n_q_heads, float *output,
+                                     void *comm, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

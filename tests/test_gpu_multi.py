@@ -28,7 +28,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, hs, lens, result_q):
+def _worker(rank, world, port, hs, lens, L, result_q):
     import datetime
     import torch
     import torch.distributed as dist
@@ -47,7 +47,7 @@ def _worker(rank, world, port, hs, lens, result_q):
         torch.cuda.set_device(rank)
         E.set_device(rank)
         dev = torch.device("cuda", rank)
-        L, nq, nkv, hd = 2, 16, 4, 128
+        nq, nkv, hd = 16, 4, 128
         ss = world // hs
         h_i, s_i = rank // ss, rank % ss
         groups = [dist.new_group(ranks=[h * ss + k for k in range(ss)]) for h in range(hs)]
@@ -55,9 +55,10 @@ def _worker(rank, world, port, hs, lens, result_q):
         datas = [kv_data(rng, L, nkv, n, hd) for n in lens]
         q = rng.standard_normal((len(lens), L, nq, hd)).astype(np.float32)
         kh, qh = nkv // hs, nq // hs
-        for b, n in enumerate(lens):
-            lo, hi = seq_shard(n, ss, s_i)
-            c = E.Cache(L, kh, hd, max(hi - lo, 1))
+        cuts = [seq_shard(n, ss, s_i) for n in lens]
+        cap = max(1, max(hi - lo for lo, hi in cuts))   # one cache shape per batch
+        for b, (lo, hi) in enumerate(cuts):
+            c = E.Cache(L, kh, hd, cap)
             if hi > lo:
                 mine = np.ascontiguousarray(datas[b][:, :, h_i * kh:(h_i + 1) * kh, lo:hi])
                 assert c.load_raw(mine, hi - lo) == 0
@@ -68,10 +69,20 @@ def _worker(rank, world, port, hs, lens, result_q):
         outs = []
         for _ in range(2):                           # two steps in a row
             do = torch.full_like(dq, float("nan"))
+            # every rank is ready before any enters the NCCL collective: a rank
+            # that failed earlier ends this host barrier with an error instead
+            # of leaving its peers waiting in the collective on the GPU
+            dist.barrier()
             dec.step(dq, do, stream=stream)
             stream.synchronize()
             outs.append(do.cpu().numpy())
         assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+        # the host-buffer form (chunked from 1 MiB of queries on) gives the same bits
+        hq = np.ascontiguousarray(q[:, :, h_i * qh:(h_i + 1) * qh])
+        ho = np.full_like(hq, np.nan)
+        dist.barrier()
+        dec.step_host(hq, ho, stream=stream)
+        assert np.array_equal(ho.view(np.uint32), outs[0].view(np.uint32)), "host form differs"
         for b, n in enumerate(lens):
             rc = O.RefCache(L, nkv, hd, n)
             rc.load_raw(datas[b], n)
@@ -91,7 +102,7 @@ def _worker(rank, world, port, hs, lens, result_q):
         dist.destroy_process_group()
 
 
-def _run(world, hs, lens):
+def _run(world, hs, lens, L=2):
     import torch
     import torch.multiprocessing as mp
     if not HAS_GPU or torch.cuda.device_count() < world:
@@ -99,7 +110,7 @@ def _run(world, hs, lens):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, hs, lens, q))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, hs, lens, L, q))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -116,10 +127,12 @@ def _run(world, hs, lens):
         assert results[r][1] == results[(r // ss) * ss][1], f"rank {r} differs from its group"
 
 
-@pytest.mark.parametrize("lens", [[1000, 333], [50, 2048]])
-def test_sequence_split_two_gpus(lens):
-    """[50, 2048]: the second rank's slice of the first sequence is empty."""
-    _run(2, 1, lens)
+@pytest.mark.parametrize("lens,L", [([1000, 333], 2), ([50, 2048], 2), ([300] * 6, 22)])
+def test_sequence_split_two_gpus(lens, L):
+    """[50, 2048]: the second rank's slice of the first sequence is empty.
+    Six caches of 22 layers: 1.1 MB of queries, so the host-buffer form runs
+    in chunks, one all-gather each."""
+    _run(2, 1, lens, L)
 
 
 def test_head_shards_times_sequence_split_four_gpus():
