@@ -119,8 +119,8 @@ int host_streams(int dev, HostStreams &hs) {
   }
   HostStreams &h = g_host_streams[dev];
   if (!h.in) {
-    cudaStream_t t[3] = {nullptr, nullptr, nullptr};
-    for (int i = 0; i < 3; i++) {
+    cudaStream_t t[4] = {nullptr, nullptr, nullptr, nullptr};
+    for (int i = 0; i < 4; i++) {
       int rc = check_cuda(cudaStreamCreateWithFlags(&t[i], cudaStreamNonBlocking),
                           "decode_attention_host: stream");
       if (rc) {
@@ -131,6 +131,7 @@ int host_streams(int dev, HostStreams &hs) {
     h.in = t[0];
     h.out = t[1];
     h.alt = t[2];
+    h.coll = t[3];
   }
   hs = h;
   return EAKV_OK;

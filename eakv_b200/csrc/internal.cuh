@@ -196,12 +196,14 @@ DecodeArgs base_args(const eakv_cache_t *c0, int n_caches, int n_q);
 void fill_batch(DecodeBatch &b, const eakv_cache_t *const *caches, int n);
 
 // Host-buffer pipelines (api.cu): helper streams per device (queries in,
-// outputs out, a second compute stream), created on first use; and the cut of
+// outputs out, a second compute stream, a collective stream), created on
+// first use; and the cut of
 // n units (caches) into up to four chunks whose copies overlap the other
 // chunks' work, a one-unit chunk first and last. Below kPipelineMinBytes of
 // queries a call is not cut.
 struct HostStreams {
   cudaStream_t in = nullptr, out = nullptr, alt = nullptr;
+  cudaStream_t coll = nullptr;   // collectives and merges of the multi-GPU split
 };
 constexpr size_t kPipelineMinBytes = 1u << 20;
 int host_streams(int dev, HostStreams &hs);

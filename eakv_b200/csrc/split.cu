@@ -104,25 +104,39 @@ size_t record_floats(size_t rows, int head_dim) {
   return (rows * (head_dim + 1) + 63) / 64 * 64;
 }
 
-// Queues one split step of batch (a, b) on stream s: the partial decode into
-// this rank's record slot, the all-gather of the records, the merge into
-// d_out. records holds world * rec floats; ws / ws_bytes are the decode's
-// split workspace (a.cnt its counters).
-int split_launch(const NcclApi *n, ncclComm_t nc, int world, int rank, DecodeArgs a,
-                 const DecodeBatch &b, float *records, size_t rec, void *ws, size_t ws_bytes,
-                 float *d_out, cudaStream_t s) {
+// The partial decode of batch (a, b) on stream s, its records going into this
+// rank's slot of `records` (world blocks of rec floats). ws / ws_bytes are the
+// decode's split workspace (a.cnt its counters).
+int partial_launch(int rank, DecodeArgs a, const DecodeBatch &b, float *records, size_t rec,
+                   void *ws, size_t ws_bytes, cudaStream_t s) {
   const size_t rows = (size_t)a.n_caches * a.n_layers * a.n_q_heads;
   float *mine = records + (size_t)rank * rec;
   a.out = mine;
   a.lse = mine + rows * a.head_dim;
-  int rc = decode_launch(a, b, ws, ws_bytes, s);
-  if (rc) return rc;
+  return decode_launch(a, b, ws, ws_bytes, s);
+}
+
+// The all-gather of the records of `rows` rows and their merge into d_out, on s.
+int gather_merge(const NcclApi *n, ncclComm_t nc, int world, int rank, size_t rows, int hd,
+                 float *records, size_t rec, float *d_out, cudaStream_t s) {
   if (world > 1) {
-    rc = check_nccl(n, n->all_gather(mine, records, rec, ncclFloat32, nc, s), "ncclAllGather");
+    float *mine = records + (size_t)rank * rec;
+    int rc = check_nccl(n, n->all_gather(mine, records, rec, ncclFloat32, nc, s), "ncclAllGather");
     if (rc) return rc;
   }
-  return lse_combine_launch(world, (int)rows, a.head_dim, records, rec, records + rows * a.head_dim,
-                            rec, d_out, nullptr, s);
+  return lse_combine_launch(world, (int)rows, hd, records, rec, records + rows * hd, rec, d_out,
+                            nullptr, s);
+}
+
+// Queues one whole split step of batch (a, b) on stream s: partial decode,
+// all-gather, merge into d_out.
+int split_launch(const NcclApi *n, ncclComm_t nc, int world, int rank, DecodeArgs a,
+                 const DecodeBatch &b, float *records, size_t rec, void *ws, size_t ws_bytes,
+                 float *d_out, cudaStream_t s) {
+  int rc = partial_launch(rank, a, b, records, rec, ws, ws_bytes, s);
+  if (rc) return rc;
+  const size_t rows = (size_t)a.n_caches * a.n_layers * a.n_q_heads;
+  return gather_merge(n, nc, world, rank, rows, a.head_dim, records, rec, d_out, s);
 }
 
 // The communicator's size, this rank, and a check that it lives on `device`.
@@ -236,16 +250,87 @@ int eakv_decode_attention_split(const eakv_cache_t *const *caches, int n_caches,
   a.pos_end = pos_end;
   DecodeBatch b;
   fill_batch(b, caches, n_caches);
-  const size_t rows = (size_t)n_caches * c0->n_layers * n_q;
-  const size_t rec = record_floats(rows, c0->head_dim);
-  // scratch: [records of every rank | decode split workspace]
-  const size_t rec_bytes = (size_t)world * rec * sizeof(float);
-  const size_t ws = decode_workspace_bytes(a, b);
-  void *base = nullptr;
-  rc = cache_workspace(c0, decode_counters(a, b), rec_bytes + ws, &a.cnt, &base);
+  const int hd = c0->head_dim;
+  const size_t unit = (size_t)c0->n_layers * n_q;   // rows of one cache
+  if (n_caches < 2) {
+    const size_t rows = (size_t)n_caches * unit;
+    const size_t rec = record_floats(rows, hd);
+    // scratch: [records of every rank | decode split workspace]
+    const size_t rec_bytes = (size_t)world * rec * sizeof(float);
+    const size_t ws = decode_workspace_bytes(a, b);
+    void *base = nullptr;
+    rc = cache_workspace(c0, decode_counters(a, b), rec_bytes + ws, &a.cnt, &base);
+    if (rc) return rc;
+    return split_launch(n, nc, world, rank, a, b, (float *)base, rec,
+                        ws ? (uint8_t *)base + rec_bytes : nullptr, ws, d_out, s);
+  }
+  // Two halves of the caches, each keeping the whole batch's split plan: the
+  // second half's partial decode runs on a second stream, so its CTAs fill
+  // the SMs as the first half's drain, and the first half's all-gather and
+  // merge run on the collective stream meanwhile; only the second half's
+  // exchange is left after the last decode. Every collective is on the
+  // collective stream, in the same order on every rank.
+  HostStreams hs;
+  rc = host_streams(c0->device, hs);
   if (rc) return rc;
-  return split_launch(n, nc, world, rank, a, b, (float *)base, rec,
-                      ws ? (uint8_t *)base + rec_bytes : nullptr, ws, d_out, s);
+  decode_fix_plan(a, b);
+  const int cut[3] = {0, n_caches / 2, n_caches};
+  DecodeArgs ca[2];
+  DecodeBatch cb[2];
+  size_t rec[2], rbytes[2], ws[2], cnt[2];
+  for (int k = 0; k < 2; k++) {
+    const int cn = cut[k + 1] - cut[k];
+    ca[k] = a;
+    ca[k].n_caches = cn;
+    ca[k].q = d_q + (size_t)cut[k] * unit * hd;
+    fill_batch(cb[k], caches + cut[k], cn);
+    rec[k] = record_floats((size_t)cn * unit, hd);
+    rbytes[k] = ((size_t)world * rec[k] * sizeof(float) + 255) / 256 * 256;
+    ws[k] = (decode_workspace_bytes(ca[k], cb[k]) + 255) / 256 * 256;
+    cnt[k] = decode_counters(ca[k], cb[k]);
+  }
+  // scratch: [records 0 | records 1 | workspace 0 | workspace 1], counters 0 then 1
+  void *vbase = nullptr;
+  unsigned *counters = nullptr;
+  rc = cache_workspace(c0, cnt[0] + cnt[1], rbytes[0] + rbytes[1] + ws[0] + ws[1], &counters,
+                       &vbase);
+  if (rc) return rc;
+  uint8_t *base = (uint8_t *)vbase;
+  float *records[2] = {(float *)base, (float *)(base + rbytes[0])};
+  void *wsp[2] = {ws[0] ? base + rbytes[0] + rbytes[1] : nullptr,
+                  ws[1] ? base + rbytes[0] + rbytes[1] + ws[0] : nullptr};
+  ca[0].cnt = counters;
+  ca[1].cnt = counters + cnt[0];
+  cudaEvent_t ev[4] = {};
+  int made = 0;
+  for (; made < 4; made++) {
+    rc = check_cuda(cudaEventCreateWithFlags(&ev[made], cudaEventDisableTiming), who);
+    if (rc) break;
+  }
+  auto step = [&](cudaError_t e) {
+    if (!rc) rc = check_cuda(e, who);
+  };
+  const cudaStream_t dec[2] = {s, hs.alt};
+  if (!rc) {
+    // both decodes and the exchange start after earlier work on s
+    step(cudaEventRecord(ev[0], s));
+    step(cudaStreamWaitEvent(hs.alt, ev[0], 0));
+    step(cudaStreamWaitEvent(hs.coll, ev[0], 0));
+    for (int k = 0; k < 2 && !rc; k++) {
+      rc = partial_launch(rank, ca[k], cb[k], records[k], rec[k], wsp[k], ws[k], dec[k]);
+      step(cudaEventRecord(ev[1 + k], dec[k]));
+    }
+    for (int k = 0; k < 2 && !rc; k++) {
+      step(cudaStreamWaitEvent(hs.coll, ev[1 + k], 0));
+      if (rc) break;
+      rc = gather_merge(n, nc, world, rank, (size_t)ca[k].n_caches * unit, hd, records[k], rec[k],
+                        d_out + (size_t)cut[k] * unit * hd, hs.coll);
+    }
+    step(cudaEventRecord(ev[3], hs.coll));
+    step(cudaStreamWaitEvent(s, ev[3], 0));   // later work on s sees the merged output
+  }
+  for (int i = 0; i < made; i++) cudaEventDestroy(ev[i]);
+  return rc;
 }
 
 int eakv_decode_attention_split_host(const eakv_cache_t *const *caches, int n_caches,
@@ -285,47 +370,62 @@ int eakv_decode_attention_split_host(const eakv_cache_t *const *caches, int n_ca
   int start[5];
   const int nch = n_caches > 1 && nfl * sizeof(float) >= kPipelineMinBytes
                       ? host_chunks(n_caches, start) : (start[0] = 0, start[1] = n_caches, 1);
-  // the largest chunk sets the records and workspace sizes; the chunks run
-  // one after another on stream s, so they share both
+  // Chunk k decodes on stream s or the second compute stream (alternately),
+  // then its all-gather and merge run on the collective stream while the
+  // next chunk decodes; its copy out waits for its merge. Chunks on one
+  // compute stream share that stream's split workspace and counters; every
+  // chunk has its own records.
   DecodeArgs ca[4];
   DecodeBatch cb[4];
-  size_t rec = 0, ws = 0, cnt = 0;
+  size_t rec[4] = {}, rbytes[4] = {}, ws = 0, cnt = 0;
   for (int k = 0; k < nch; k++) {
     const int cn = start[k + 1] - start[k];
     ca[k] = a;
     ca[k].n_caches = cn;
     fill_batch(cb[k], caches + start[k], cn);
-    const size_t r = record_floats((size_t)cn * c0->n_layers * n_q, hd);
+    rec[k] = record_floats((size_t)cn * c0->n_layers * n_q, hd);
+    rbytes[k] = ((size_t)world * rec[k] * sizeof(float) + 255) / 256 * 256;
     const size_t w = decode_workspace_bytes(ca[k], cb[k]);
     const size_t c = decode_counters(ca[k], cb[k]);
-    if (r > rec) rec = r;
     if (w > ws) ws = w;
     if (c > cnt) cnt = c;
   }
+  ws = (ws + 255) / 256 * 256;
   const size_t half = (nfl * sizeof(float) + 255) / 256 * 256;
-  const size_t rec_bytes = ((size_t)world * rec * sizeof(float) + 255) / 256 * 256;
+  size_t rec_total = 0;
+  for (int k = 0; k < nch; k++) rec_total += rbytes[k];
+  // scratch: [queries | outputs | records of each chunk | workspace of s | of the second stream]
   void *vbase = nullptr;
   unsigned *counters = nullptr;
-  rc = cache_workspace(c0, cnt, 2 * half + rec_bytes + ws, &counters, &vbase);
+  rc = cache_workspace(c0, 2 * cnt, 2 * half + rec_total + 2 * ws, &counters, &vbase);
   if (rc) return rc;
   uint8_t *base = (uint8_t *)vbase;
   float *dq = (float *)base, *dout = (float *)(base + half);
-  float *records = (float *)(base + 2 * half);
-  void *wsp = ws ? base + 2 * half + rec_bytes : nullptr;
+  float *records[4];
+  {
+    uint8_t *r = base + 2 * half;
+    for (int k = 0; k < nch; k++) {
+      records[k] = (float *)r;
+      r += rbytes[k];
+    }
+  }
+  uint8_t *wsp = base + 2 * half + rec_total;
 
-  cudaEvent_t ev[9] = {};
+  cudaEvent_t ev[13] = {};
   int made = 0;
-  for (; made < 2 * nch + 1; made++) {
+  for (; made < 3 * nch + 1; made++) {
     rc = check_cuda(cudaEventCreateWithFlags(&ev[made], cudaEventDisableTiming), who);
     if (rc) break;
   }
-  cudaEvent_t ev0 = ev[0], *ev_in = ev + 1, *ev_done = ev + 1 + nch;
+  cudaEvent_t ev0 = ev[0], *ev_in = ev + 1, *ev_dec = ev + 1 + nch, *ev_done = ev + 1 + 2 * nch;
   auto step = [&](cudaError_t e) {
     if (!rc) rc = check_cuda(e, who);
   };
   if (!rc) {
     step(cudaEventRecord(ev0, s));
     step(cudaStreamWaitEvent(hs.in, ev0, 0));
+    step(cudaStreamWaitEvent(hs.alt, ev0, 0));
+    step(cudaStreamWaitEvent(hs.coll, ev0, 0));
     for (int k = 0; k < nch && !rc; k++) {
       const size_t off = start[k] * unit, len = (start[k + 1] - start[k]) * unit;
       step(cudaMemcpyAsync(dq + off, queries + off, len * sizeof(float), cudaMemcpyHostToDevice,
@@ -334,12 +434,22 @@ int eakv_decode_attention_split_host(const eakv_cache_t *const *caches, int n_ca
     }
     for (int k = 0; k < nch && !rc; k++) {
       const size_t off = start[k] * unit;
-      step(cudaStreamWaitEvent(s, ev_in[k], 0));
+      const cudaStream_t ds = (k & 1) ? hs.alt : s;
+      step(cudaStreamWaitEvent(ds, ev_in[k], 0));
       if (rc) break;
       ca[k].q = dq + off;
-      ca[k].cnt = counters;
-      rc = split_launch(n, nc, world, rank, ca[k], cb[k], records, rec, wsp, ws, dout + off, s);
-      step(cudaEventRecord(ev_done[k], s));
+      ca[k].cnt = counters + (k & 1) * cnt;
+      rc = partial_launch(rank, ca[k], cb[k], records[k], rec[k], ws ? wsp + (k & 1) * ws : nullptr,
+                          ws, ds);
+      step(cudaEventRecord(ev_dec[k], ds));
+    }
+    for (int k = 0; k < nch && !rc; k++) {
+      const size_t off = start[k] * unit;
+      step(cudaStreamWaitEvent(hs.coll, ev_dec[k], 0));
+      if (rc) break;
+      rc = gather_merge(n, nc, world, rank, (size_t)ca[k].n_caches * c0->n_layers * n_q, hd,
+                        records[k], rec[k], dout + off, hs.coll);
+      step(cudaEventRecord(ev_done[k], hs.coll));
     }
     for (int k = 0; k < nch && !rc; k++) {
       const size_t off = start[k] * unit, len = (start[k + 1] - start[k]) * unit;
@@ -349,7 +459,7 @@ int eakv_decode_attention_split_host(const eakv_cache_t *const *caches, int n_ca
     }
   }
   // nothing of this call is left in flight when it returns, error or not
-  const cudaStream_t all[3] = {hs.in, s, hs.out};
+  const cudaStream_t all[5] = {hs.in, s, hs.alt, hs.coll, hs.out};
   for (cudaStream_t t : all) {
     cudaError_t e = cudaStreamSynchronize(t);
     if (!rc && e != cudaSuccess) rc = check_cuda(e, who);
