@@ -797,7 +797,8 @@ def run_twocall(args, world, rank, local):
             fn()
         return (time.perf_counter() - t0) / reps * 1e3
 
-    for name, L, nq, nkv, hd, S in TWOCALL_SHAPES:
+    shapes = TWOCALL_SHAPES if args.shape < 0 else [TWOCALL_SHAPES[args.shape]]
+    for name, L, nq, nkv, hd, S in shapes:
         data = rng.standard_normal((L, 2, nkv, S, hd), dtype=np.float32)
         c = E.Cache(L, nkv, hd, S)
         c.set_stream(stream.cuda_stream)
@@ -820,7 +821,7 @@ def run_twocall(args, world, rank, local):
             fsize = os.path.getsize(path)
             ms_fload = wall(lambda: E.Cache.load(path).free(), 3)
             cpu = {}
-            if R is not None:
+            if R is not None and not args.no_cpu:
                 rc_ = R.eakv_cache_create(L, nkv, hd, S)
                 sc = np.zeros(nq * S, np.float32)
                 out = np.zeros(nq * hd, np.float32)
@@ -959,6 +960,8 @@ def main():
                     help="time another part instead: the reference's two-call attention API "
                          "and its load_raw / save / load, the q4_1_eakv ggml type kernels, "
                          "device validate + dequantize, or the llama.cpp state import")
+    ap.add_argument("--shape", type=int, default=-1,
+                    help="--op twocall: only this entry of its shape list (0-3; 3 is one cfg4 layer)")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)

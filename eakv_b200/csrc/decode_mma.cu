@@ -306,7 +306,8 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
     for (int n = 0; n < C::VNT; n++)
 #pragma unroll
       for (int r = 0; r < 4; r++) dv[i][n][r] = 0.0f;
-  float m_run = -INFINITY, l_run = 0.0f;
+  float m_run = -INFINITY, m_eff = 0.0f;   // m_eff: m_run, or 0 while it is -inf
+  float2 l2 = make_float2(0.0f, 0.0f);       // sum of p, two running halves
   float pb[NG];
 #pragma unroll
   for (int gg = 0; gg < NG; gg++) pb[gg] = 0.0f;
@@ -399,15 +400,19 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
     }
 
     // ---- online softmax (base 2, lazy max) ----------------------------------
-    float tmax = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
-    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
-    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
-    const bool need = tmax > m_run + 8.0f;
-    if (__any_sync(0xffffffffu, need)) {
+    // The row's running max moves only when a score passes it by more than 8;
+    // each lane tests its own four scores, and only then (rarely) is the
+    // row's max formed across the quad.
+    const float lmax = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+    if (__any_sync(0xffffffffu, lmax > m_run + 8.0f)) {
+      float tmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, 1));
+      tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
+      const bool need = tmax > m_run + 8.0f;
       const float m_new = need ? tmax : m_run;
       const float alpha = need ? ex2(m_run - m_new) : 1.0f;   // exp2(-inf) = 0
       m_run = m_new;
-      l_run *= alpha;
+      m_eff = m_run == -INFINITY ? 0.0f : m_run;
+      l2 = __fmul2_rn(l2, make_float2(alpha, alpha));
 #pragma unroll
       for (int gg = 0; gg < NG; gg++) pb[gg] *= alpha;
 #pragma unroll
@@ -422,13 +427,14 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
           }
       }
     }
-    const float m_eff = m_run == -INFINITY ? 0.0f : m_run;
-    float p[4];
+    float p[4], pf[4];
 #pragma unroll
     for (int j = 0; j < 4; j++) {
       p[j] = ex2(sc[j] - m_eff);
-      l_run += p[j];
+      pf[j] = p[j] * fs;   // exact: fs is a power of two
     }
+    l2 = __fadd2_rn(l2, make_float2(p[0], p[1]));
+    l2 = __fadd2_rn(l2, make_float2(p[2], p[3]));
 
     // ---- P' fragments and the V contraction, group by group ------------------
 #pragma unroll
@@ -436,21 +442,19 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
       float ps[4];
 #pragma unroll
       for (int j = 0; j < 4; j++) {
-        ps[j] = p[j] * (sv[j][gg] * fs);
+        ps[j] = pf[j] * sv[j][gg];
         pb[gg] = fmaf(p[j], bv[j][gg], pb[gg]);
       }
-      uint32_t bh0, bl0, bh1, bl1;   // limbs of positions (2c, 2c+1) and (2c+8, 2c+9)
-      split2(ps[0], ps[1], bh0, bl0);
-      split2(ps[2], ps[3], bh1, bl1);
-      uint32_t b0[C::VNT], b1[C::VNT];
+      uint32_t b0[C::VNT], b1[C::VNT];   // positions (2c, 2c+1) and (2c+8, 2c+9)
       if (C::VNT == 1) {
-        b0[0] = my_limb ? bl0 : bh0;
-        b1[0] = my_limb ? bl1 : bh1;
+        uint32_t h0, l0, h1, l1;   // this lane's limb of each pair
+        split2(ps[0], ps[1], h0, l0);
+        split2(ps[2], ps[3], h1, l1);
+        b0[0] = my_limb ? l0 : h0;
+        b1[0] = my_limb ? l1 : h1;
       } else {
-        b0[0] = bh0;
-        b1[0] = bh1;
-        b0[C::VNT - 1] = bl0;
-        b1[C::VNT - 1] = bl1;
+        split2(ps[0], ps[1], b0[0], b0[C::VNT - 1]);
+        split2(ps[2], ps[3], b1[0], b1[C::VNT - 1]);
       }
       // V nibbles of the step's 16 positions, as four transposed 8x8 b16
       // tiles: tile 2w + blk holds positions p0 + 8 blk .. + 7 (rows) and
@@ -535,6 +539,7 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
   }
 
   // ---- per-warp totals --------------------------------------------------------
+  float l_run = l2.x + l2.y;
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
 #pragma unroll

@@ -137,3 +137,64 @@ def test_sequence_split_two_gpus(lens, L):
 
 def test_head_shards_times_sequence_split_four_gpus():
     _run(4, 2, [1500, 700])
+
+
+def _worker_lost(rank, world, port, result_q):
+    """Rank 1 leaves after one good step (no destroy, no further collective).
+    Rank 0 learns it at the host barrier before its next step (gloo, 10 s),
+    never enters the collective, and ends its communicator with
+    eakv_nccl_comm_abort."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=10))
+    import eakv_b200 as E
+    from eakv_b200.parallel import SeqSplitDecoder
+    from gpu_util import kv_data
+    torch.cuda.set_device(rank)
+    E.set_device(rank)
+    rng = np.random.default_rng(3)
+    L, nq, nkv, hd, S = 1, 8, 2, 128, 256
+    c = E.Cache(L, nkv, hd, S)
+    assert c.load_raw(kv_data(rng, L, nkv, S, hd), S) == 0
+    dec = SeqSplitDecoder([c], nq, hd, device=rank)
+    dq = torch.from_numpy(rng.standard_normal((1, L, nq, hd)).astype(np.float32)).to(rank)
+    do = torch.empty_like(dq)
+    stream = torch.cuda.Stream(rank)
+    dist.barrier()
+    dec.step(dq, do, stream=stream)               # one good step
+    stream.synchronize()
+    if rank == 1:
+        result_q.put((rank, "left"))
+        result_q.close()
+        result_q.join_thread()
+        os._exit(0)                                # gone between steps
+    try:
+        dist.barrier()                             # the host learns of it here
+        result_q.put((rank, "no error"))
+    except Exception as e:                         # noqa: BLE001 - any error ends the wait
+        dec.comm.abort()                           # no collective of it is in flight
+        result_q.put((rank, f"raised {type(e).__name__}, aborted"))
+    c.free()
+
+
+def test_lost_rank_between_steps_two_gpus():
+    import torch
+    import torch.multiprocessing as mp
+    if not HAS_GPU or torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_lost, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert results[1] == "left"
+    assert results[0].startswith("raised") and results[0].endswith("aborted"), results[0]
