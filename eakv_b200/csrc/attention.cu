@@ -196,12 +196,12 @@ cudaError_t launch_scores_hd(dim3 grid, const PageGeom &g, const uint8_t *d_buf,
 
 constexpr int kVHeads = 8;          // query heads per block (accumulators per thread)
 constexpr int kVThreads = 128;
-constexpr int kVChunkPages = 16;    // positions of one block: 1024
+constexpr int kVChunkPages = 8;     // positions of one block: 512
 constexpr int kVExactMax = 512;     // up to this length the whole sum is one chain
 
 // V sum. Every output element (query head h, dim d) is its own chain over
 // positions, o = fma(fma(n, s, b), w[h][t], o), in position order
-// (kernels/fused_v_sum.ea:111-150). A block takes up to 16 pages of one KV
+// (kernels/fused_v_sum.ea:111-150). A block takes up to 8 pages of one KV
 // head and up to 8 query heads: one bulk copy per page brings the pages into
 // shared memory (one mbarrier, bounded wait), the weights are staged beside
 // them, and the positions are cut among position streams of HD/8 threads.
