@@ -80,3 +80,16 @@ def test_create_rejects_bad_params_without_device():
     assert L.eakv_cache_compression_ratio(None) == 0.0
     assert L.eakv_checkpoint(None) == 0
     assert L.eakv_restore(None, 0) == E.EAKV_ERR_INVALID
+
+
+def test_nccl_is_resolved_at_run_time():
+    """The multi-GPU calls (include/eakv_nccl.h) find NCCL at run time, with
+    no link dependency: the library reports the loaded NCCL's version and
+    makes unique ids (128 bytes, a new one per call) without a GPU."""
+    import eakv_b200 as E
+    assert E.nccl_version() >= 21000
+    a, b = E.nccl_unique_id(), E.nccl_unique_id()
+    assert len(a) == E.NCCL_ID_BYTES == 128 and a != b
+    import subprocess
+    out = subprocess.run(["ldd", E.LIB_PATH], capture_output=True, text=True).stdout
+    assert "nccl" not in out
