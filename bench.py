@@ -393,7 +393,10 @@ def run_b200(args, cfg, world, rank, local):
     if split:
         from eakv_b200.parallel import SeqSplitDecoder
         decoder = SeqSplitDecoder(caches, nq, hd, group=sub, device=local)
-        launches_per_step += 1   # the merge kernel after the all-gather
+        # the library decodes two halves of the caches, each followed by its
+        # merge kernel after the all-gather (one of each for a single cache)
+        launches_per_step = 2 * (launches_per_step + 1) if len(caches) > 1 \
+            else launches_per_step + 1
 
     appending = bool(cfg.get("append"))
     if appending:

@@ -55,11 +55,16 @@ int eakv_nccl_comm_abort(void *comm);
  * order of calls; every rank receives in d_output
  * (f32[n_caches][n_layers][n_q_heads][head_dim]) the softmax attention over
  * the union of the slices. Per rank: the partial decode of positions
- * [pos_begin, min(pos_end, seq_len)) of its caches (0, -1: all), one
- * ncclAllGather of the records (n_caches * n_layers * n_q_heads *
- * (head_dim + 1) floats per rank), and the exact merge, all queued on
- * `stream` (NULL: the first cache's stream); nothing synchronizes the host.
- * Workspace comes from the first cache's scratch. */
+ * [pos_begin, min(pos_end, seq_len)) of its caches (0, -1: all), an
+ * ncclAllGather of the records (n_layers * n_q_heads * (head_dim + 1) floats
+ * per cache and rank), and the exact merge. With two or more caches the
+ * caches are taken in two halves: the second half decodes on a second
+ * stream while the first half's all-gather and merge run on a collective
+ * stream of the library, so two all-gathers are issued per call. Everything
+ * is ordered after earlier work on `stream` (NULL: the first cache's
+ * stream), later work on `stream` sees the output, and nothing synchronizes
+ * the host. Workspace comes from the first cache's scratch; the helper
+ * streams are shared by the calls of one device. */
 int eakv_decode_attention_split(const eakv_cache_t *const *caches, int n_caches,
                                 const float *d_queries, int n_q_heads, int pos_begin,
                                 int pos_end, float *d_output, void *comm, void *stream);

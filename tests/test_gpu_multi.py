@@ -198,3 +198,44 @@ def test_lost_rank_between_steps_two_gpus():
         p.join(timeout=60)
     assert results[1] == "left"
     assert results[0].startswith("raised") and results[0].endswith("aborted"), results[0]
+
+
+def test_c_host_split_two_gpus(tmp_path):
+    """The library's multi-GPU split from a plain C host (tests/c/split_c_host.c):
+    no Python in the ranks, the NCCL id passed through a file, host buffers
+    only; each rank checks the merged result against a single-GPU decode of
+    the whole sequences within 1e-4."""
+    import shutil
+    import subprocess
+    import sys
+    import torch
+    if not HAS_GPU or torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if not cc:
+        pytest.skip("no C compiler")
+    import eakv_b200 as E
+    from conftest import ROOT
+    libdir = os.path.dirname(E.LIB_PATH)
+    exe = str(tmp_path / "split_c_host")
+    subprocess.run([cc, "-O2", "-Wall", "-I", os.path.join(ROOT, "include"),
+                    os.path.join(ROOT, "tests", "c", "split_c_host.c"), "-L", libdir,
+                    "-leakv_b200", f"-Wl,-rpath,{libdir}", "-lm", "-o", exe], check=True)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    idf = str(tmp_path / "nccl.id")
+    procs = [subprocess.Popen([exe, str(r), "2", idf], stdout=subprocess.PIPE,
+                              stderr=subprocess.PIPE, text=True, env=env) for r in range(2)]
+    outs = []
+    for p in procs:
+        try:
+            o, e = p.communicate(timeout=300)
+        except subprocess.TimeoutExpired:
+            for pp in procs:
+                pp.kill()
+            raise
+        outs.append((p.returncode, o, e))
+    for r, (rc, o, e) in enumerate(outs):
+        sys.stderr.write(e)
+        # NCCL may print its version banner on stdout first
+        last = o.strip().splitlines()[-1] if o.strip() else ""
+        assert rc == 0 and last.startswith("ok"), f"rank {r}: rc {rc} {o!r} {e!r}"
