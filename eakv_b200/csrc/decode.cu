@@ -27,6 +27,8 @@
 
 #include <atomic>
 
+#include <vector>
+
 #include "internal.cuh"
 #include "pipeline.cuh"
 #include "decode_common.cuh"
@@ -506,27 +508,48 @@ constexpr int kMaxSplitPages = 256;   // 16384 positions
 // us, at 16: 35.0 us), whose ranking it reproduces.
 constexpr double kCtaOverheadPages = 8.0;
 
-static double split_cost(long long items, int max_pages, int ns, int per_sm, int sms) {
-  const int sp = (max_pages + ns - 1) / ns;
+// frac[r] = (r / per_sm)^(2/3), the cost of a last round of r CTAs.
+static double split_cost(long long items, int max_pages, int sp, int per_sm, int sms,
+                         const double *frac) {
   const int n = (max_pages + sp - 1) / sp;
   const long long m = (items * n + sms - 1) / sms;
   const long long rounds = (m + per_sm - 1) / per_sm;
   const long long r = m - (long long)per_sm * (rounds - 1);
-  return (sp + kCtaOverheadPages) * ((double)(rounds - 1) + pow((double)r / per_sm, 2.0 / 3.0));
+  return (sp + kCtaOverheadPages) * ((double)(rounds - 1) + frac[r]);
 }
 
 // The split count in [lo, hi] of least modeled duration (the first of equals).
+// Split counts with the same split length cost the same, so only the first
+// count of each length is evaluated; and since decode steps repeat their
+// shapes, each host thread keeps its last few answers.
 int choose_splits(long long items, int max_pages, int lo, int hi, int per_sm, int sms) {
   if (max_pages < 1 || lo < 1 || hi < lo || per_sm < 1 || sms < 1) return lo > 0 ? lo : 1;
+  struct Memo {
+    long long items;
+    int max_pages, lo, hi, per_sm, sms, ns;
+  };
+  thread_local Memo memo[4] = {};
+  thread_local int memo_next = 0;
+  for (const Memo &m : memo)
+    if (m.ns && m.items == items && m.max_pages == max_pages && m.lo == lo && m.hi == hi &&
+        m.per_sm == per_sm && m.sms == sms)
+      return m.ns;
+  std::vector<double> frac(per_sm + 1);
+  for (int r = 0; r <= per_sm; r++) frac[r] = pow((double)r / per_sm, 2.0 / 3.0);
   int ns = lo;
-  double best = split_cost(items, max_pages, lo, per_sm, sms);
-  for (int k = lo + 1; k <= hi; k++) {
-    const double c = split_cost(items, max_pages, k, per_sm, sms);
-    if (c < best) {
+  double best = 0.0;
+  for (int k = lo; k <= hi;) {
+    const int sp = (max_pages + k - 1) / k;
+    const double c = split_cost(items, max_pages, sp, per_sm, sms, frac.data());
+    if (k == lo || c < best) {
       best = c;
       ns = k;
     }
+    if (sp == 1) break;
+    k = (max_pages - 1) / (sp - 1) + 1;   // the first count whose splits are shorter
   }
+  memo[memo_next] = Memo{items, max_pages, lo, hi, per_sm, sms, ns};
+  memo_next = (memo_next + 1) % 4;
   return ns;
 }
 

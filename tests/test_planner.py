@@ -50,3 +50,42 @@ def test_planner_bounds_and_degenerate_inputs():
     assert E.choose_splits(100, 64, 5, 5, 4, SMS) == 5      # a single candidate
     assert E.choose_splits(100, 64, 3, 2, 4, SMS) == 3      # empty range: the lower bound
     assert E.choose_splits(0, 64, 1, 32, 4, SMS) >= 1
+
+
+def _model_choice(items, max_pages, lo, hi, per_sm, sms):
+    """The makespan model evaluated at every split count in [lo, hi] (the
+    first of equal costs wins): the reference for the library's shortcut,
+    which evaluates one count per split length and remembers recent answers."""
+    best, ns = None, lo
+    for k in range(lo, hi + 1):
+        sp = -(-max_pages // k)
+        n = -(-max_pages // sp)
+        m = -(-(items * n) // sms)
+        rounds = -(-m // per_sm)
+        r = m - per_sm * (rounds - 1)
+        c = (sp + 8.0) * ((rounds - 1) + (r / per_sm) ** (2.0 / 3.0))
+        if best is None or c < best:
+            best, ns = c, k
+    return ns
+
+
+def test_planner_shortcut_equals_the_full_scan():
+    import random
+
+    import eakv_b200 as E
+    rnd = random.Random(7)
+    cases = [(items, pages, 1, pages, per_sm)
+             for items in (1, 8, 88, 256, 1024, 4096)
+             for pages in (1, 2, 3, 7, 32, 129, 512, 2048)
+             for per_sm in (1, 3, 4)]
+    cases += [(rnd.randint(1, 20000), rnd.randint(1, 3000), 0, 0, rnd.randint(1, 8))
+              for _ in range(300)]
+    for items, pages, lo, hi, per_sm in cases:
+        if hi == 0:
+            lo = rnd.randint(1, pages)
+            hi = rnd.randint(lo, pages)
+        want = _model_choice(items, pages, lo, hi, per_sm, SMS)
+        # twice: the second answer comes from the per-thread memo
+        for _ in range(2):
+            assert E.choose_splits(items, pages, lo, hi, per_sm, SMS) == want, \
+                (items, pages, lo, hi, per_sm)
