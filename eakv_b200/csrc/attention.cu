@@ -20,6 +20,7 @@
 #include <stdio.h>
 
 #include <atomic>
+#include <type_traits>
 
 #include "internal.cuh"
 #include "pipeline.cuh"
@@ -139,33 +140,45 @@ scores_kernel(const uint8_t *__restrict__ buf, PageGeom g, int layer,
         dequant4((z1 >> 4) & 0x0F0F0F0Fu, s2, b2, k[p][grp][3][0], k[p][grp][3][1]);
       }
     }
-    for (int j = 0; j < nh; j++) {
-      float2 acc[2][2];
+    // NP query heads at once: 4 NP independent f32x2 chains per thread
+    auto score_heads = [&](int j, auto np_tag) {
+      constexpr int NP = decltype(np_tag)::value;
+      float2 acc[NP][2][2];
 #pragma unroll
-      for (int p = 0; p < 2; p++) acc[p][0] = acc[p][1] = make_float2(0.0f, 0.0f);
+      for (int u = 0; u < NP; u++)
+#pragma unroll
+        for (int p = 0; p < 2; p++) acc[u][p][0] = acc[u][p][1] = make_float2(0.0f, 0.0f);
 #pragma unroll
       for (int grp = 0; grp < GPD; grp++)
 #pragma unroll
-        for (int jj = 0; jj < 4; jj++) {
-          const float4 qv = q_s[((j * GPD + grp) * 4 + jj) * 4 + t];
-          const float2 qa = make_float2(qv.x, qv.y), qb = make_float2(qv.z, qv.w);
+        for (int jj = 0; jj < 4; jj++)
 #pragma unroll
-          for (int p = 0; p < 2; p++) {
-            acc[p][0] = __ffma2_rn(k[p][grp][jj][0], qa, acc[p][0]);
-            acc[p][1] = __ffma2_rn(k[p][grp][jj][1], qb, acc[p][1]);
+          for (int u = 0; u < NP; u++) {
+            const float4 qv = q_s[(((j + u) * GPD + grp) * 4 + jj) * 4 + t];
+            const float2 qa = make_float2(qv.x, qv.y), qb = make_float2(qv.z, qv.w);
+#pragma unroll
+            for (int p = 0; p < 2; p++) {
+              acc[u][p][0] = __ffma2_rn(k[p][grp][jj][0], qa, acc[u][p][0]);
+              acc[u][p][1] = __ffma2_rn(k[p][grp][jj][1], qb, acc[u][p][1]);
+            }
           }
-        }
 #pragma unroll
-      for (int p = 0; p < 2; p++) {
-        const float2 t1 = __fadd2_rn(acc[p][0], acc[p][1]);   // lanes l + l+8
-        float r = __fadd_rn(t1.x, t1.y);                       // l + l+4
-        r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 2));  // l + l+2
-        r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 1));  // l + l+1
-        const int gpos = pg0 * kPagePositions + tp[p];
-        if (t == 0 && tp[p] < pos_end && gpos < seq_len)
-          scores[(size_t)(kvh * q_per_kv + h0 + j) * seq_len + gpos] = __fmul_rn(r, rsqrt_d);
-      }
-    }
+      for (int u = 0; u < NP; u++)
+#pragma unroll
+        for (int p = 0; p < 2; p++) {
+          const float2 t1 = __fadd2_rn(acc[u][p][0], acc[u][p][1]);   // lanes l + l+8
+          float r = __fadd_rn(t1.x, t1.y);                             // l + l+4
+          r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 2));        // l + l+2
+          r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 1));        // l + l+1
+          const int gpos = pg0 * kPagePositions + tp[p];
+          if (t == 0 && tp[p] < pos_end && gpos < seq_len)
+            scores[(size_t)(kvh * q_per_kv + h0 + j + u) * seq_len + gpos] = __fmul_rn(r, rsqrt_d);
+        }
+    };
+    int j = 0;
+    for (; j + 3 < nh; j += 4) score_heads(j, std::integral_constant<int, 4>{});
+    for (; j + 1 < nh; j += 2) score_heads(j, std::integral_constant<int, 2>{});
+    if (j < nh) score_heads(j, std::integral_constant<int, 1>{});
   }
 }
 
@@ -198,6 +211,21 @@ constexpr int kVHeads = 8;          // query heads per block (accumulators per t
 constexpr int kVThreads = 128;
 constexpr int kVChunkPages = 8;     // positions of one block: 512
 constexpr int kVExactMax = 512;     // up to this length the whole sum is one chain
+constexpr int kVMergeInLaunch = 32; // most blocks per sequence merged inside the launch
+
+// A block's arrival at its item's counter, after its partial sums are
+// written: true in the item's last block to arrive. The counter wraps back
+// to zero with that arrival, ready for the next launch.
+__device__ __forceinline__ bool vsum_arrive_last(unsigned *cnt, int n) {
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicInc(cnt, (unsigned)n - 1) == (unsigned)n - 1;
+  __syncthreads();
+  const bool last = s_last != 0;
+  if (last) __threadfence();
+  return last;
+}
 
 // V sum. Every output element (query head h, dim d) is its own chain over
 // positions, o = fma(fma(n, s, b), w[h][t], o), in position order
@@ -214,22 +242,24 @@ constexpr int kVExactMax = 512;     // up to this length the whole sum is one ch
 //
 // grid: (chunks of kVChunkPages pages, n_kv, head groups of kVHeads).
 // Writes d_out directly when there is one chunk, else a partial per chunk.
-template <int HD>
+template <int HD, int NH>
 __global__ void __launch_bounds__(kVThreads)
 vsum_kernel(const uint8_t *__restrict__ buf, PageGeom g, int layer,
-            const float *__restrict__ w, int q_per_kv, int seq_len, int n_chunks,
-            float *__restrict__ out, float *__restrict__ part, int n_q, int *status) {
+            const float *__restrict__ w, int q_per_kv, int seq_len, int cp, int n_chunks,
+            float *__restrict__ out, float *__restrict__ part, unsigned *__restrict__ cnt,
+            int n_q, int *status) {
   constexpr int GPD = HD / 64, TPS = HD / 8, NSTREAM = kVThreads / TPS;
   constexpr int PB = kPagePositions * GPD * 40, NIB = kPagePositions * GPD * 32;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t *bar = reinterpret_cast<uint64_t *>(smem);
   uint8_t *pages = smem + 128;
-  float *w_s = reinterpret_cast<float *>(pages + kVChunkPages * PB);   // [kVHeads][1024]
+  float *w_s = reinterpret_cast<float *>(pages + cp * PB);   // [nh][cp * 64]
   const int kvh = blockIdx.y;
   const int h0 = blockIdx.z * kVHeads;
   const int nh = min(kVHeads, q_per_kv - h0);
-  const int c0 = blockIdx.x * kVChunkPages * kPagePositions;
-  const int len = min(seq_len - c0, kVChunkPages * kPagePositions);
+  const int cpos = cp * kPagePositions;   // positions of a block
+  const int c0 = blockIdx.x * cpos;
+  const int len = min(seq_len - c0, cpos);
   const int pg0 = c0 / kPagePositions, npg = (len + kPagePositions - 1) / kPagePositions;
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(bar), 1);
@@ -256,7 +286,7 @@ vsum_kernel(const uint8_t *__restrict__ buf, PageGeom g, int layer,
     for (int u = 0; u < 8; u++) {
       const int i = i0 + u * kVThreads + threadIdx.x;
       const int j = i / len, tt = i - j * len;
-      if (i < nh * len) w_s[j * kVChunkPages * kPagePositions + tt] = wv[u];
+      if (i < nh * len) w_s[j * cpos + tt] = wv[u];
     }
   }
   const bool ok = mbar_wait(smem_u32(bar), 0, kWaitBudget);
@@ -265,21 +295,58 @@ vsum_kernel(const uint8_t *__restrict__ buf, PageGeom g, int layer,
       if (status) atomicOr(status, kStatusWaitTimeout);
       mbar_wait(smem_u32(bar), 0, kWaitBudget);   // no copy may outlive the block
     }
+    // arrive all the same, so that the counter returns to zero (the status
+    // word tells the caller the result is void)
+    if (cnt) vsum_arrive_last(cnt + blockIdx.y * gridDim.z + blockIdx.z, n_chunks);
     return;
   }
   const int stream = threadIdx.x / TPS, i = threadIdx.x - stream * TPS;
   const int nused = seq_len <= kVExactMax ? 1 : NSTREAM;
-  const int sub = (len + nused - 1) / nused;
+  // streams take runs of a multiple of 4 positions (16-byte weight loads)
+  const int sub = ((len + nused - 1) / nused + 3) & ~3;
   const int t0 = stream * sub, t1 = min(len, t0 + sub);
   const int grp = (4 * i) / 32;
-  float2 o[kVHeads][4];
+  float2 o[NH][4];
 #pragma unroll
-  for (int j = 0; j < kVHeads; j++)
+  for (int j = 0; j < NH; j++)
 #pragma unroll
     for (int k = 0; k < 4; k++) o[j][k] = make_float2(0.0f, 0.0f);
   if (stream < nused) {
-#pragma unroll 4
-    for (int tt = t0; tt < t1; tt++) {
+    // four positions at a time (one page: 4 divides 64), their loads first;
+    // every accumulator still takes its positions in order
+    int tt = t0;
+    for (; tt + 4 <= t1; tt += 4) {
+      const uint8_t *pp = pages + (tt / kPagePositions) * PB;
+      const int pip = tt % kPagePositions;
+      uint32_t wd[4];
+      float2 sb[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        wd[u] = *reinterpret_cast<const uint32_t *>(pp + (pip + u) * (HD / 2) + 4 * i);
+        sb[u] = *reinterpret_cast<const float2 *>(pp + NIB + ((pip + u) * GPD + grp) * 8);
+      }
+      float2 v[4][4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const float2 s2 = make_float2(sb[u].x, sb[u].x), b2 = make_float2(sb[u].y, sb[u].y);
+        dequant4(wd[u] & 0x0F0F0F0Fu, s2, b2, v[u][0], v[u][1]);
+        dequant4((wd[u] >> 4) & 0x0F0F0F0Fu, s2, b2, v[u][2], v[u][3]);
+      }
+#pragma unroll
+      for (int j = 0; j < NH; j++) {
+        if (j < nh) {
+          const float4 w4 = *reinterpret_cast<const float4 *>(w_s + j * cpos + tt);
+          const float wu[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            const float2 w2 = make_float2(wu[u], wu[u]);
+#pragma unroll
+            for (int k = 0; k < 4; k++) o[j][k] = __ffma2_rn(v[u][k], w2, o[j][k]);
+          }
+        }
+      }
+    }
+    for (; tt < t1; tt++) {
       const uint8_t *pp = pages + (tt / kPagePositions) * PB;
       const int pip = tt % kPagePositions;
       const uint32_t word = *reinterpret_cast<const uint32_t *>(pp + pip * (HD / 2) + 4 * i);
@@ -289,9 +356,9 @@ vsum_kernel(const uint8_t *__restrict__ buf, PageGeom g, int layer,
       dequant4(word & 0x0F0F0F0Fu, s2, b2, v[0], v[1]);
       dequant4((word >> 4) & 0x0F0F0F0Fu, s2, b2, v[2], v[3]);
 #pragma unroll
-      for (int j = 0; j < kVHeads; j++) {
+      for (int j = 0; j < NH; j++) {
         if (j < nh) {
-          const float wj = w_s[j * kVChunkPages * kPagePositions + tt];
+          const float wj = w_s[j * cpos + tt];
           const float2 w2 = make_float2(wj, wj);
 #pragma unroll
           for (int k = 0; k < 4; k++) o[j][k] = __ffma2_rn(v[k], w2, o[j][k]);
@@ -304,40 +371,57 @@ vsum_kernel(const uint8_t *__restrict__ buf, PageGeom g, int layer,
   float *dst = n_chunks == 1 ? out : part + (size_t)blockIdx.x * n_q * HD;
   if (nused == 1) {
     if (stream == 0) {
-      for (int j = 0; j < nh; j++) {
-        float *r = dst + (size_t)(kvh * q_per_kv + h0 + j) * HD + dim0;
-        *reinterpret_cast<float4 *>(r) = make_float4(o[j][0].x, o[j][0].y, o[j][1].x, o[j][1].y);
-        *reinterpret_cast<float4 *>(r + 32) =
-            make_float4(o[j][2].x, o[j][2].y, o[j][3].x, o[j][3].y);
+#pragma unroll
+      for (int j = 0; j < NH; j++) {
+        if (j < nh) {
+          float *r = dst + (size_t)(kvh * q_per_kv + h0 + j) * HD + dim0;
+          *reinterpret_cast<float4 *>(r) =
+              make_float4(o[j][0].x, o[j][0].y, o[j][1].x, o[j][1].y);
+          *reinterpret_cast<float4 *>(r + 32) =
+              make_float4(o[j][2].x, o[j][2].y, o[j][3].x, o[j][3].y);
+        }
       }
     }
     return;
   }
   // add the streams' sums in position order, through shared memory
   __syncthreads();   // the pages are no longer read
-  float *acc_s = reinterpret_cast<float *>(pages);   // [NSTREAM][kVHeads][HD]
-  for (int j = 0; j < nh; j++) {
-    float *r = acc_s + (stream * kVHeads + j) * HD + dim0;
-    *reinterpret_cast<float4 *>(r) = make_float4(o[j][0].x, o[j][0].y, o[j][1].x, o[j][1].y);
-    *reinterpret_cast<float4 *>(r + 32) = make_float4(o[j][2].x, o[j][2].y, o[j][3].x, o[j][3].y);
+  float *acc_s = reinterpret_cast<float *>(smem + 128);   // [NSTREAM][nh][HD]
+#pragma unroll
+  for (int j = 0; j < NH; j++) {
+    if (j < nh) {
+      float *r = acc_s + (stream * nh + j) * HD + dim0;
+      *reinterpret_cast<float4 *>(r) = make_float4(o[j][0].x, o[j][0].y, o[j][1].x, o[j][1].y);
+      *reinterpret_cast<float4 *>(r + 32) =
+          make_float4(o[j][2].x, o[j][2].y, o[j][3].x, o[j][3].y);
+    }
   }
   __syncthreads();
   for (int e = threadIdx.x; e < nh * HD; e += kVThreads) {
     const int j = e / HD, d = e - j * HD;
     float a = acc_s[j * HD + d];
-    for (int st = 1; st < NSTREAM; st++) a = __fadd_rn(a, acc_s[(st * kVHeads + j) * HD + d]);
+    for (int st = 1; st < NSTREAM; st++) a = __fadd_rn(a, acc_s[(st * nh + j) * HD + d]);
     dst[(size_t)(kvh * q_per_kv + h0 + j) * HD + d] = a;
   }
-}
-
-// out[i] = part[0][i] + part[1][i] + ... in chunk order.
-__global__ void vsum_combine_kernel(const float *__restrict__ part, int n_chunks, size_t n,
-                                   float *__restrict__ out) {
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (size_t)gridDim.x * blockDim.x) {
-    float acc = part[i];
-    for (int c = 1; c < n_chunks; c++) acc = __fadd_rn(acc, part[(size_t)c * n + i]);
-    out[i] = acc;
+  // the last block of this (KV head, head group) adds the blocks' sums in
+  // chunk order (L1 bypassed: the other blocks wrote them from other SMs),
+  // eight loads in flight at a time
+  if (cnt && vsum_arrive_last(cnt + blockIdx.y * gridDim.z + blockIdx.z, n_chunks)) {
+    const size_t n = (size_t)n_q * HD;
+    for (int e = threadIdx.x; e < nh * HD; e += kVThreads) {
+      const float *pr = part + (size_t)(kvh * q_per_kv + h0) * HD + e;
+      float a = __ldcg(pr);
+      int c = 1;
+      for (; c + 8 <= n_chunks; c += 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) v[u] = __ldcg(pr + (size_t)(c + u) * n);
+#pragma unroll
+        for (int u = 0; u < 8; u++) a = __fadd_rn(a, v[u]);
+      }
+      for (; c < n_chunks; c++) a = __fadd_rn(a, __ldcg(pr + (size_t)c * n));
+      out[(size_t)(kvh * q_per_kv + h0) * HD + e] = a;
+    }
   }
 }
 
@@ -347,34 +431,88 @@ __global__ void fill_kernel(float *p, size_t n, float v) {
     p[i] = v;
 }
 
-int vsum_chunks(int seq_len) {
-  const int per = kVChunkPages * kPagePositions;
-  return seq_len > 0 ? (seq_len + per - 1) / per : 1;
+// out[i] = part[0][i] + part[1][i] + ... in chunk order (the same order as
+// the merge inside the launch).
+__global__ void vsum_combine_kernel(const float *__restrict__ part, int n_chunks, size_t n,
+                                    float *__restrict__ out) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    float acc = part[i];
+    for (int c = 1; c < n_chunks; c++) acc = __fadd_rn(acc, part[(size_t)c * n + i]);
+    out[i] = acc;
+  }
 }
 
-template <int HD>
-size_t vsum_smem() {
-  return 128 + (size_t)kVChunkPages * kPagePositions * (HD / 64) * 40 +
-         (size_t)kVHeads * kVChunkPages * kPagePositions * sizeof(float);
+// Pages of one block. Up to kVExactMax positions the whole sequence is one
+// block (its single stream keeps the reference's order, bit for bit); beyond
+// that, blocks of 1..kVChunkPages pages, about one block per SM when the
+// call is small (each block pays a fixed set-up and adds one partial sum),
+// so that short sequences still spread over the GPU.
+int vsum_chunk_pages(int n_q, int n_kv, int seq_len) {
+  const int pages = (seq_len + kPagePositions - 1) / kPagePositions;
+  if (seq_len <= kVExactMax) return pages > 0 ? pages : 1;
+  const int q_per_kv = n_q / n_kv;
+  const long long blocks = (long long)pages * n_kv * ((q_per_kv + kVHeads - 1) / kVHeads);
+  const long long cp = (blocks + 147) / 148;
+  return (int)(cp < 1 ? 1 : cp > kVChunkPages ? kVChunkPages : cp);
 }
 
+int vsum_chunks(int n_q, int n_kv, int seq_len) {
+  if (seq_len <= 0) return 1;
+  const int cp = vsum_chunk_pages(n_q, n_kv, seq_len);
+  return (seq_len + cp * kPagePositions - 1) / (cp * kPagePositions);
+}
+
+// Shared memory of a block with nh query heads and cp pages: the staged
+// pages and the heads' weights, later reused for the streams' sums. Sized by
+// the heads and pages a block really has, so that 4 query heads per KV head
+// fit 4 blocks per SM.
 template <int HD>
-cudaError_t launch_vsum_hd(dim3 grid, const PageGeom &g, const uint8_t *d_buf, int layer,
-                           const float *d_w, int q_per_kv, int seq_len, int n_chunks, float *d_out,
-                           float *d_part, int n_q, int *status, cudaStream_t s) {
+size_t vsum_smem(int nh, int cp) {
+  const size_t staged = (size_t)cp * kPagePositions * (HD / 64) * 40 +
+                        (size_t)nh * cp * kPagePositions * sizeof(float);
+  const size_t sums = (size_t)(kVThreads / (HD / 8)) * nh * HD * sizeof(float);
+  return 128 + (staged > sums ? staged : sums);
+}
+
+template <int HD, int NH>
+cudaError_t launch_vsum_nh(dim3 grid, const PageGeom &g, const uint8_t *d_buf, int layer,
+                           const float *d_w, int q_per_kv, int seq_len, int cp, int n_chunks,
+                           float *d_out, float *d_part, unsigned *d_cnt, int n_q, int *status,
+                           cudaStream_t s) {
   static std::atomic<unsigned long long> attr_done{0};   // one bit per device
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(attr_done.load(std::memory_order_acquire) >> (dev & 63) & 1)) {
-    cudaError_t e = cudaFuncSetAttribute(vsum_kernel<HD>,
+    cudaError_t e = cudaFuncSetAttribute(vsum_kernel<HD, NH>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)vsum_smem<HD>());
+                                         (int)vsum_smem<HD>(NH, kVChunkPages));
     if (e != cudaSuccess) return e;
     attr_done.fetch_or(1ull << (dev & 63), std::memory_order_acq_rel);
   }
-  vsum_kernel<HD><<<grid, kVThreads, vsum_smem<HD>(), s>>>(d_buf, g, layer, d_w, q_per_kv, seq_len,
-                                                           n_chunks, d_out, d_part, n_q, status);
+  const int nh = q_per_kv < NH ? q_per_kv : NH;
+  vsum_kernel<HD, NH><<<grid, kVThreads, vsum_smem<HD>(nh, cp), s>>>(
+      d_buf, g, layer, d_w, q_per_kv, seq_len, cp, n_chunks, d_out, d_part, d_cnt, n_q, status);
   return cudaGetLastError();
+}
+
+// The kernel's head count: the smallest of 1, 2, 4, 8 that holds a block's
+// query heads (min(q_per_kv, kVHeads)), so that its accumulators fit.
+template <int HD>
+cudaError_t launch_vsum_hd(dim3 grid, const PageGeom &g, const uint8_t *d_buf, int layer,
+                           const float *d_w, int q_per_kv, int seq_len, int cp, int n_chunks,
+                           float *d_out, float *d_part, unsigned *d_cnt, int n_q, int *status,
+                           cudaStream_t s) {
+  const int nh = q_per_kv < kVHeads ? q_per_kv : kVHeads;
+  auto go = [&](auto nh_tag) {
+    return launch_vsum_nh<HD, decltype(nh_tag)::value>(grid, g, d_buf, layer, d_w, q_per_kv,
+                                                        seq_len, cp, n_chunks, d_out, d_part,
+                                                        d_cnt, n_q, status, s);
+  };
+  if (nh <= 1) return go(std::integral_constant<int, 1>{});
+  if (nh <= 2) return go(std::integral_constant<int, 2>{});
+  if (nh <= 4) return go(std::integral_constant<int, 4>{});
+  return go(std::integral_constant<int, 8>{});
 }
 
 }  // namespace
@@ -401,35 +539,44 @@ cudaError_t launch_scores(const PageGeom &g, const uint8_t *d_buf, int layer, co
                                     d_scores, ppb, status, s);
 }
 
-size_t vsum_scratch_floats(const PageGeom &g, int n_q, int seq_len) {
-  const int n_chunks = vsum_chunks(seq_len);
+size_t vsum_scratch_floats(const PageGeom &g, int n_q, int n_kv, int seq_len) {
+  const int n_chunks = vsum_chunks(n_q, n_kv, seq_len);
   return n_chunks > 1 ? (size_t)n_chunks * n_q * g.gpd * 64 : 0;
+}
+
+size_t vsum_counters(int n_q, int n_kv, int seq_len) {
+  const int n_chunks = vsum_chunks(n_q, n_kv, seq_len);
+  return n_chunks > 1 && n_chunks <= kVMergeInLaunch
+             ? (size_t)n_kv * ((n_q / n_kv + kVHeads - 1) / kVHeads) : 0;
 }
 
 cudaError_t launch_vsum(const PageGeom &g, const uint8_t *d_buf, int layer, const float *d_w,
                         int n_q, int n_kv, int seq_len, float *d_out, float *d_part,
-                        size_t part_floats, cudaStream_t s) {
+                        size_t part_floats, unsigned *d_cnt, cudaStream_t s) {
   const int head_dim = g.gpd * 64;
   if (seq_len <= 0) {   // reference stores the zero-initialized accumulators
     fill_kernel<<<32, 256, 0, s>>>(d_out, (size_t)n_q * head_dim, 0.0f);
     return cudaGetLastError();
   }
   const int q_per_kv = n_q / n_kv;
-  const int n_chunks = vsum_chunks(seq_len);
-  if (n_chunks > 1 && (size_t)n_chunks * n_q * head_dim > part_floats)
-    return cudaErrorInvalidValue;   // the caller sizes the partials with vsum_scratch_floats
+  const int cp = vsum_chunk_pages(n_q, n_kv, seq_len);
+  const int n_chunks = vsum_chunks(n_q, n_kv, seq_len);
+  if (n_chunks > 1 && ((size_t)n_chunks * n_q * head_dim > part_floats ||
+                        (n_chunks <= kVMergeInLaunch && !d_cnt)))
+    return cudaErrorInvalidValue;   // sized by vsum_scratch_floats and vsum_counters
   dim3 grid(n_chunks, n_kv, (q_per_kv + kVHeads - 1) / kVHeads);
   int *status = device_status_ptr();
+  // few blocks per sequence: the last one adds their sums in the same launch;
+  // many: a second kernel spreads those sums over the whole GPU
+  unsigned *merge_cnt = n_chunks > 1 && n_chunks <= kVMergeInLaunch ? d_cnt : nullptr;
   cudaError_t e = head_dim == 128
-                      ? launch_vsum_hd<128>(grid, g, d_buf, layer, d_w, q_per_kv, seq_len, n_chunks,
-                                            d_out, d_part, n_q, status, s)
-                      : launch_vsum_hd<64>(grid, g, d_buf, layer, d_w, q_per_kv, seq_len, n_chunks,
-                                           d_out, d_part, n_q, status, s);
-  if (e != cudaSuccess) return e;
-  if (n_chunks > 1) {
-    size_t n = (size_t)n_q * head_dim;
-    vsum_combine_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(d_part, n_chunks, n, d_out);
-  }
+                      ? launch_vsum_hd<128>(grid, g, d_buf, layer, d_w, q_per_kv, seq_len, cp,
+                                            n_chunks, d_out, d_part, merge_cnt, n_q, status, s)
+                      : launch_vsum_hd<64>(grid, g, d_buf, layer, d_w, q_per_kv, seq_len, cp,
+                                           n_chunks, d_out, d_part, merge_cnt, n_q, status, s);
+  if (e != cudaSuccess || n_chunks <= kVMergeInLaunch) return e;
+  const size_t n = (size_t)n_q * head_dim;
+  vsum_combine_kernel<<<(int)((n + 255) / 256), 256, 0, s>>>(d_part, n_chunks, n, d_out);
   return cudaGetLastError();
 }
 
@@ -515,14 +662,17 @@ int eakv_attention_output_device(const eakv_cache_t *c, const float *d_w, int la
   int rc = attn_check(c, d_w, d_out, layer, n_q, n_kv, "attention_output");
   if (rc) return rc;
   DeviceGuard g(c->device);
-  size_t pf = vsum_scratch_floats(c->geom, n_q, c->seq_len);
+  size_t pf = vsum_scratch_floats(c->geom, n_q, n_kv, c->seq_len);
   float *d_part = nullptr;
+  unsigned *d_cnt = nullptr;
   if (pf) {
-    d_part = (float *)cache_scratch(c, pf * sizeof(float));
-    if (!d_part) return EAKV_ERR_ALLOC;
+    void *p = nullptr;
+    rc = cache_workspace(c, vsum_counters(n_q, n_kv, c->seq_len), pf * sizeof(float), &d_cnt, &p);
+    if (rc) return rc;
+    d_part = (float *)p;
   }
   return check_cuda(launch_vsum(c->geom, c->d_buf, layer, d_w, n_q, n_kv, c->seq_len, d_out,
-                                d_part, pf, c->stream),
+                                d_part, pf, d_cnt, c->stream),
                     "attention_output");
 }
 
@@ -535,20 +685,23 @@ void eakv_attention_output(const eakv_cache_t *c, const float *weights, int laye
   }
   DeviceGuard g(c->device);
   size_t nw = (size_t)n_q * c->seq_len, no = (size_t)n_q * c->head_dim;
-  size_t pf = vsum_scratch_floats(c->geom, n_q, c->seq_len);
+  size_t pf = vsum_scratch_floats(c->geom, n_q, n_kv, c->seq_len);
   size_t nw_pad = (nw + 63) / 64 * 64, no_pad = (no + 63) / 64 * 64;
-  float *d_w = (float *)cache_scratch(c, (nw_pad + no_pad + pf) * sizeof(float));
-  if (!d_w) {
+  void *p = nullptr;
+  unsigned *d_cnt = nullptr;
+  if (cache_workspace(c, vsum_counters(n_q, n_kv, c->seq_len),
+                      (nw_pad + no_pad + pf) * sizeof(float), &d_cnt, &p) != EAKV_OK) {
     fill_nan_host(output_out, no);
     return;
   }
+  float *d_w = (float *)p;
   float *d_o = d_w + nw_pad;
   float *d_part = pf ? d_o + no_pad : nullptr;
   if ((nw && check_cuda(cudaMemcpyAsync(d_w, weights, nw * sizeof(float),
                                         cudaMemcpyHostToDevice, c->stream),
                         "attention_output: copy")) ||
       check_cuda(launch_vsum(c->geom, c->d_buf, layer, d_w, n_q, n_kv, c->seq_len, d_o, d_part,
-                             pf, c->stream), "attention_output") ||
+                             pf, d_cnt, c->stream), "attention_output") ||
       check_cuda(cudaMemcpyAsync(output_out, d_o, no * sizeof(float), cudaMemcpyDeviceToHost,
                                  c->stream), "attention_output: copy") ||
       check_cuda(cudaStreamSynchronize(c->stream), "attention_output")) {

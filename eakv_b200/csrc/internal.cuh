@@ -132,8 +132,10 @@ cudaError_t launch_scores(const PageGeom &g, const uint8_t *d_buf, int layer,
 cudaError_t launch_vsum(const PageGeom &g, const uint8_t *d_buf, int layer,
                         const float *d_w, int n_q, int n_kv, int seq_len,
                         float *d_out, float *d_part, size_t part_floats,
-                        cudaStream_t s);
-size_t vsum_scratch_floats(const PageGeom &g, int n_q, int seq_len);
+                        unsigned *d_cnt, cudaStream_t s);
+size_t vsum_scratch_floats(const PageGeom &g, int n_q, int n_kv, int seq_len);
+// zeroed counters the V-sum needs when its sequence spans several blocks
+size_t vsum_counters(int n_q, int n_kv, int seq_len);
 
 // ---- decode.cu (fused flash-decoding) ----
 constexpr int kMaxBatch = 256;

@@ -80,6 +80,34 @@ def test_subset_kv_heads_and_uniform_weights(gpu):
         assert np.array_equal(bits(c.output(w, 0, 4, 4)), bits(rc.output(w, 0, 4, 4)))
 
 
+@pytest.mark.parametrize("S", [513, 1000, 4097])
+@pytest.mark.parametrize("H,nq,nkv", [(8, 8, 8), (8, 32, 8), (8, 4, 4)])
+def test_chunked_v_sum(gpu, S, H, nq, nkv):
+    """Beyond 512 positions the V-sum runs in blocks of 1..8 pages chosen
+    from the call's size (more, shorter blocks for short sequences), and the
+    last block of each head group adds the blocks' sums in order: within the
+    tolerance of the reference's single chain, also when n_kv is below the
+    cache's head count. The blocks meet at counters in the cache's workspace,
+    which the fused decode uses too: a decode between two V-sums leaves the
+    second one bit-identical to the first."""
+    L, hd = 1, 128
+    rng = np.random.default_rng(S * 3 + nq)
+    data = kv_data(rng, L, H, S, hd)
+    rc = O.RefCache(L, H, hd, S)
+    rc.load_raw(data, S)
+    with E.Cache(L, H, hd, S) as c:
+        assert c.load_raw(data, S) == 0
+        q = rng.standard_normal(nq * hd).astype(np.float32)
+        w = O.softmax_rows(rc.scores(q, 0, nq, nkv), nq, S)
+        o1 = c.output(w, 0, nq, nkv)
+        assert_close(o1, rc.output(w, 0, nq, nkv), what=f"V-sum S={S}")
+        if nkv == H:
+            c.fused(q, 0, nq, nkv)
+        o2 = c.output(w, 0, nq, nkv)
+        assert np.array_equal(bits(o1), bits(o2)), "repeated V-sum differs"
+    assert E.device_status(0) == 0
+
+
 def test_device_entry_points(gpu):
     import torch
     L, nq, nkv, hd, S = 1, 16, 4, 128, 200
