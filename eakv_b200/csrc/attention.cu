@@ -432,13 +432,21 @@ __global__ void fill_kernel(float *p, size_t n, float v) {
 }
 
 // out[i] = part[0][i] + part[1][i] + ... in chunk order (the same order as
-// the merge inside the launch).
+// the merge inside the launch), eight loads in flight at a time.
 __global__ void vsum_combine_kernel(const float *__restrict__ part, int n_chunks, size_t n,
                                     float *__restrict__ out) {
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x) {
     float acc = part[i];
-    for (int c = 1; c < n_chunks; c++) acc = __fadd_rn(acc, part[(size_t)c * n + i]);
+    int c = 1;
+    for (; c + 8 <= n_chunks; c += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) v[u] = part[(size_t)(c + u) * n + i];
+#pragma unroll
+      for (int u = 0; u < 8; u++) acc = __fadd_rn(acc, v[u]);
+    }
+    for (; c < n_chunks; c++) acc = __fadd_rn(acc, part[(size_t)c * n + i]);
     out[i] = acc;
   }
 }
