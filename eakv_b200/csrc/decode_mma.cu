@@ -202,6 +202,21 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
   const uint8_t *kpages = batch.base[it.b] + page_index(a.geom, it.layer, 0, it.h, 0) * C::PB;
   const uint8_t *vpages = kpages + kv_stride * C::PB;
 
+  // The set-up's own global loads go out first (this CTA's queries and the
+  // V-exponent entry), so that their latency overlaps the barrier set-up and
+  // the first page requests: with few CTAs per SM the set-up is on the
+  // launch's critical path.
+  const int qh0 = it.h * G + it.hg * gh;
+  const float *qb = a.q + ((size_t)(it.b * a.n_layers + it.lrow) * a.n_q_heads + qh0) * HD;
+  constexpr int QPT = (RH * HD + C::THREADS - 1) / C::THREADS;   // query elements per thread
+  float qv[QPT];
+#pragma unroll
+  for (int k = 0; k < QPT; k++) {
+    const int i = threadIdx.x + k * C::THREADS;
+    qv[k] = i < gh * HD ? __ldg(qb + i) : 0.0f;
+  }
+  const int vexp_raw = __ldg(vexp_table(batch.base[it.b], a.geom) + it.layer * a.geom.n_heads + it.h);
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::NSTAGE; s++) {
       mbar_init(smem_u32(&bars[s]), 1);                               // stage filled
@@ -226,8 +241,6 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
     for (int i = 0; i < it.npages && i < C::NSTAGE; i++) issue(i);
 
   // ---- per-thread query fragments -----------------------------------------
-  const int qh0 = it.h * G + it.hg * gh;
-  const float *qb = a.q + ((size_t)(it.b * a.n_layers + it.lrow) * a.n_q_heads + qh0) * HD;
   // Score rows: row g of m-tile mt is (head h_mine, digit l_row + 2 mt),
   // row g+8 the next digit. With 4 heads, lanes g and g^4 share a head
   // (digits 0,1 and 2,3); with 8, m-tiles 0 and 1 give lane g all four.
@@ -237,7 +250,11 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
   // stage the scaled query block; one warp per head computes max|q| and
   // the per-group sums (for the bias term)
   // (heads gh..RH-1 are idle: zero queries, results never written)
-  for (int i = threadIdx.x; i < RH * HD; i += C::THREADS) q_s[i] = i < gh * HD ? qb[i] * qscale : 0.0f;
+#pragma unroll
+  for (int k = 0; k < QPT; k++) {
+    const int i = threadIdx.x + k * C::THREADS;
+    if (i < RH * HD) q_s[i] = qv[k] * qscale;
+  }
   __syncthreads();
   for (int h = warp; h < RH; h += C::NW) {
     float mx = 0.0f;
@@ -313,8 +330,7 @@ decode_mma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ 
   for (int gg = 0; gg < NG; gg++) pb[gg] = 0.0f;
   // Every V scale of this (layer, head) is below 2^(vexp - 126) (the cache's
   // exponent table), so P' = p * s * 2^(127 - vexp) < 2 p <= 512 stays in f16.
-  const int vexp = min(max(vexp_table(batch.base[it.b], a.geom)[it.layer * a.geom.n_heads + it.h], 1),
-                       253);
+  const int vexp = min(max(vexp_raw, 1), 253);
   const float fs = __uint_as_float((uint32_t)(254 - vexp) << 23);   // 2^(127 - vexp)
   // head of each P'/output column this thread holds: n = 2c + e
   int hcol[2];
