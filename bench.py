@@ -41,6 +41,8 @@ sys.path.insert(0, ROOT)
 
 METRIC = "Q4 decode-attention KV tokens/s per GPU; achieved HBM GB/s vs B200 peak"
 UNIT = "KV tokens/s"
+# decode kernel selection (eakv_test_force_path codes)
+PATH_CODES = {"auto": 0, "simt": 1, "mma": 2, "umma": 3}
 
 CONFIGS = {
     1: dict(workload="cfg1 README MHA 8/8 heads d128 S2048 B1", L=1, nq=8, nkv=8, hd=128,
@@ -350,8 +352,7 @@ def run_b200(args, cfg, world, rank, local):
     import eakv_b200 as E
     torch.cuda.set_device(local)
     E.set_device(local)
-    if args.force_simt:
-        E.force_path(1)
+    E.force_path(PATH_CODES[args.path])
     if args.splits:
         E.force_splits(args.splits)
     if args.separate_merge:
@@ -568,9 +569,12 @@ def run_b200(args, cfg, world, rank, local):
     peak, peak_kind = measured_peak()
     achieved = alg_bytes_launch / (avg_launch_ms / 1e3) / 1e9
     G = nq // lcfg["nkv"]
-    if not args.force_simt and hd in (64, 128):
+    if args.path != "simt" and hd in (64, 128):
         gh = max(d for d in range(1, min(G, 8) + 1) if G % d == 0)   # query heads per CTA
-        kname = f"decode_mma_kernel<{hd},{8 if gh > 4 else 4}>"
+        if args.path == "umma" and hd == 128:
+            kname = f"decode_umma_kernel<{8 if gh > 4 else 4}>"
+        else:
+            kname = f"decode_mma_kernel<{hd},{8 if gh > 4 else 4}>"
     else:
         gc = 8 if G % 8 == 0 else 4 if G % 4 == 0 else 2 if G % 2 == 0 else 1
         kname = f"decode_simt_kernel<{hd},{gc}>"
@@ -972,7 +976,10 @@ def main():
                     help="override sequences per GPU (smaller cases for profiling)")
     ap.add_argument("--seq", type=int, default=0, help="override cached positions")
     ap.add_argument("--force-simt", action="store_true",
-                    help="time the CUDA-core decode kernel even where tensor cores apply")
+                    help="same as --path simt")
+    ap.add_argument("--path", default="auto", choices=list(PATH_CODES),
+                    help="decode kernel: automatic choice, the CUDA-core kernel, the mma.sync "
+                         "tensor-core kernel or the tcgen05 kernel")
     ap.add_argument("--seq-shards", type=int, default=0,
                     help="sharded configs: ranks per sequence split (0: the config's "
                          "choice - cfg4 two, cfg5 as many KV-head shards as divide the "
@@ -989,6 +996,8 @@ def main():
     ap.add_argument("--splits", type=int, default=0,
                     help="force this many sequence splits per row (0: planner's choice)")
     args = ap.parse_args()
+    if args.force_simt:
+        args.path = "simt"
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     cfg = dict(CONFIGS[args.config])

@@ -484,7 +484,9 @@ def separate_merge(on):
 
 
 def force_path(path):
-    """1: CUDA-core decode kernel for every shape; 0: automatic choice."""
+    """Decode kernel of later calls on this thread: 1 the CUDA-core kernel, 2 the
+    mma.sync tensor-core kernel, 3 the tcgen05 tensor-core kernel (head_dim
+    128), 0 the automatic choice."""
     lib().eakv_test_force_path(int(path))
 
 

@@ -510,7 +510,7 @@ extern "C" int eakv_test_choose_splits(long long items, int max_pages, int lo, i
 }
 
 extern "C" int eakv_test_force_path(int path) {
-  eakv::t_force_path = path == 1 ? 1 : 0;
+  eakv::t_force_path = (path >= 1 && path <= 3) ? path : 0;
   return EAKV_OK;
 }
 

@@ -490,6 +490,7 @@ int resident_gc(int gc) {
 // CUDA-core kernel when forced) and the split count.
 struct Plan {
   int mma_gh;   // 0: CUDA-core kernel
+  bool umma;    // tcgen05 kernel (else mma.sync) for the tensor-core path
   int gc;       // query heads per CTA
   int items;
 };
@@ -572,6 +573,7 @@ static Plan plan(DecodeArgs &a, const DecodeBatch &batch) {
   Plan p;
   p.mma_gh = a.force_path == 1 ? 0 : mma_heads_per_cta(G, a.head_dim);
   p.gc = p.mma_gh ? p.mma_gh : pick_gc(G);
+  p.umma = p.mma_gh && a.force_path == 3 && umma_resident(p.mma_gh, a.head_dim) > 0;
   int max_pages = 0;
   for (int i = 0; i < a.n_caches; i++) {
     int r0 = a.pos_begin > 0 ? a.pos_begin : 0;
@@ -587,8 +589,9 @@ static Plan plan(DecodeArgs &a, const DecodeBatch &batch) {
     a.n_splits = a.fix_n_splits;
     return p;
   }
-  const int resident = p.mma_gh ? mma_resident(p.mma_gh, a.head_dim)
-                                : (a.head_dim == 128 ? resident_gc<128>(p.gc) : resident_gc<64>(p.gc));
+  const int resident = p.umma     ? umma_resident(p.mma_gh, a.head_dim)
+                       : p.mma_gh ? mma_resident(p.mma_gh, a.head_dim)
+                                  : (a.head_dim == 128 ? resident_gc<128>(p.gc) : resident_gc<64>(p.gc));
   int ns = 1;
   if (max_pages > 1) {
     // fewest splits: the tensor core's f32 accumulators drift with the
@@ -658,7 +661,9 @@ int decode_launch(const DecodeArgs &a0, const DecodeBatch &batch, void *workspac
   const int n_blocks = p.items * a.n_splits;
   if (n_blocks <= 0) return EAKV_OK;
   int rc;
-  if (p.mma_gh)
+  if (p.umma)
+    rc = umma_launch(p.mma_gh, a, batch, n_blocks, s);
+  else if (p.mma_gh)
     rc = mma_launch(p.mma_gh, a, batch, n_blocks, s);
   else
     rc = a.head_dim == 128 ? dispatch_gc<128>(p.gc, a, batch, n_blocks, s)

@@ -155,7 +155,8 @@ struct DecodeArgs {
   float *lse;                       // optional [cache][layer][q_head] natural-log LSE
   int *status;                      // device status word (bounded waits)
   int force_splits;                 // > 0: use this many splits (tests)
-  int force_path;                   // 1: CUDA-core kernel even where tensor cores apply
+  int force_path;                   // 1: CUDA-core kernel even where tensor cores apply;
+                                    // 2: mma.sync tensor-core kernel; 3: tcgen05 kernel
   unsigned wait_budget;             // polls per bounded wait (0: the default budget)
   int test_stall;                   // > 0: page test_stall-1 of every item is never
                                     // requested, so its wait runs out (tests only)
@@ -214,6 +215,10 @@ int host_chunks(int n, int (&start)[5]);
 int mma_heads_per_cta(int G, int head_dim);   // 0 when the head_dim is not served
 int mma_resident(int gh, int head_dim);
 int mma_launch(int gh, const DecodeArgs &a, const DecodeBatch &b, int n_blocks, cudaStream_t s);
+// decode_umma.cu: tcgen05 decode (head_dim 128, up to 8 query heads per CTA);
+// umma_resident is 0 where it is not served
+int umma_resident(int gh, int head_dim);
+int umma_launch(int gh, const DecodeArgs &a, const DecodeBatch &b, int n_blocks, cudaStream_t s);
 extern thread_local int t_force_path;
 extern thread_local int t_force_splits;
 extern thread_local int t_test_stall;

@@ -55,6 +55,26 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint32_
   return false;
 }
 
+// Bounded wait that suspends instead of spinning: each try may sleep up to
+// about 2 us and returns as soon as the phase completes; at most `budget`
+// tries. For waits that are expected to take a while (a warp waiting on
+// tensor-core work or on other warps), so that the waiting warp does not
+// take issue slots from the warps doing the work.
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, uint32_t budget) {
+  for (uint32_t i = 0; i < budget; i++) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(2000u)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+
 // Bounded wait until page i has been requested into its stage (last = the
 // stage's "last page requested" slot). Only then is the stage's barrier in
 // page i's phase: a consumer that waited on the phase parity earlier, while

@@ -190,10 +190,11 @@ int eakv_test_force_splits(int n);
 int eakv_test_choose_splits(long long items, int max_pages, int lo, int hi, int per_sm,
                             int sms);
 
-/* path 1 makes later fused / decode calls on this host thread use the
- * CUDA-core kernel even for shapes the tensor-core kernel serves (GQA
- * groups of 4 or 8); 0 restores the automatic choice. For tests and
- * side-by-side measurements. */
+/* Kernel choice of later fused / decode calls on this host thread, for tests
+ * and side-by-side measurements: 1 the CUDA-core kernel even for shapes the
+ * tensor-core kernels serve, 2 the mma.sync tensor-core kernel (the automatic
+ * choice), 3 the tcgen05 tensor-core kernel (head_dim 128; other shapes keep
+ * the automatic choice); 0 restores the automatic choice. */
 int eakv_test_force_path(int path);
 
 /* on != 0 makes later decode calls on this host thread merge their sequence

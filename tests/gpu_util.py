@@ -91,3 +91,8 @@ def assert_close(got, ref, atol=1e-4, rtol=1e-4, what=""):
         raise AssertionError(f"{what}: {bad.sum()} of {bad.size} outside tolerance; worst at {i}: "
                              f"got {got.flat[i]!r} ref {ref.flat[i]!r} err {err.flat[i]:.3e}")
     return float(err.max()) if err.size else 0.0
+
+
+# decode kernel selection for E.force_path: the automatic choice, the
+# CUDA-core kernel, the mma.sync tensor-core kernel, the tcgen05 kernel
+PATH_CODE = {"auto": 0, "simt": 1, "mma": 2, "umma": 3}

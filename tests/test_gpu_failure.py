@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 
 import eakv_b200 as E
-from gpu_util import assert_close, kv_data
+from gpu_util import PATH_CODE, assert_close, kv_data
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -28,10 +28,10 @@ def _reset_hooks():
     E.force_path(0)
 
 
-@pytest.mark.parametrize("path", ["auto", "simt"])
+@pytest.mark.parametrize("path", ["auto", "simt", "mma", "umma"])
 @pytest.mark.parametrize("splits,page", [(0, 0), (1, 5), (3, 1)])
 def test_wait_timeout_sets_status(gpu, path, splits, page):
-    E.force_path(1 if path == "simt" else 0)
+    E.force_path(PATH_CODE[path])
     E.force_splits(splits)
     L, nq, nkv, hd, S = 1, 16, 4, 128, 1000     # 16 pages per head
     rng = np.random.default_rng(7 + page)

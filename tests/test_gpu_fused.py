@@ -6,7 +6,7 @@ import pytest
 
 import eakv_b200 as E
 from conftest import golden
-from gpu_util import assert_close, kv_data
+from gpu_util import PATH_CODE, assert_close, kv_data
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -21,9 +21,10 @@ def _reset_splits():
     E.force_path(0)
 
 
-# "auto" runs the tensor-core kernel for 4 or 8 query heads per KV head and
-# the CUDA-core kernel otherwise; "simt" forces the CUDA-core kernel
-PATHS = ["auto", "simt"]
+# "auto" is the library's own choice; "simt" forces the CUDA-core kernel,
+# "mma" the mma.sync tensor-core kernel and "umma" the tcgen05 kernel (shapes
+# a forced kernel does not serve fall back to the automatic choice)
+PATHS = ["auto", "simt", "mma", "umma"]
 
 
 @pytest.mark.parametrize("name", ["mha128", "gqa64_8to2", "gqa128_4to1", "mha64"])
@@ -53,7 +54,7 @@ CASES = [
 @pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("L,nq,nkv,hd,S,maxS", CASES)
 def test_fused_random(gpu, L, nq, nkv, hd, S, maxS, path):
-    E.force_path(1 if path == "simt" else 0)
+    E.force_path(PATH_CODE[path])
     rng = np.random.default_rng(S * 7 + nq)
     data = kv_data(rng, L, nkv, S, hd)
     rc = O.RefCache(L, nkv, hd, maxS)
@@ -69,7 +70,7 @@ def test_fused_random(gpu, L, nq, nkv, hd, S, maxS, path):
 @pytest.mark.parametrize("splits", [1, 2, 3, 7, 64])
 def test_forced_splits(gpu, splits, path):
     """Split + exact LSE combine gives the same result as one pass."""
-    E.force_path(1 if path == "simt" else 0)
+    E.force_path(PATH_CODE[path])
     L, nq, nkv, hd, S = 1, 16, 4, 128, 1111
     rng = np.random.default_rng(splits)
     data = kv_data(rng, L, nkv, S, hd)
@@ -85,7 +86,7 @@ def test_forced_splits(gpu, splits, path):
 @pytest.mark.parametrize("path", PATHS)
 def test_large_scores_softmax_stability(gpu, path):
     """Queries scaled x30: scores in the hundreds, softmax near one-hot."""
-    E.force_path(1 if path == "simt" else 0)
+    E.force_path(PATH_CODE[path])
     L, nq, nkv, hd, S = 1, 8, 2, 128, 500
     rng = np.random.default_rng(77)
     data = kv_data(rng, L, nkv, S, hd)
@@ -289,7 +290,7 @@ def test_split_merge_in_kernel_equals_separate_pass(gpu, path, L, nq, nkv, hd, l
     same bits. Three calls in a row: every call returns the split counters to
     zero, so each call merges exactly once per row group."""
     import torch
-    E.force_path(1 if path == "simt" else 0)
+    E.force_path(PATH_CODE[path])
     rng = np.random.default_rng(sum(lens) + nq)
     maxS = max(lens)
     caches = []
