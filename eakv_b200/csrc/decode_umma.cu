@@ -24,20 +24,24 @@
 //
 // Outputs. The same trick with V as the A operand (rows = the 64 nibble
 // bytes of a position, then their masked high nibbles; MN-major, positions
-// along K) and the weights as B: P' = p * s_v * 2^(127 - vexp) * 2^23 < 2^32
+// along K) and the weights as B: P' = p * s_v * 2^(127 - vexp) * 2^29 < 2^32
 // becomes an unsigned 32-bit fixed-point integer whose four bytes are its
 // base-256 digits, i.e. the thread stores the integers as they are. The s32
 // accumulators are exact (a digit column gains at most 255 * 255 per
 // position, below 2^31 for 33025 positions; splits are at most 16384), so
-// the only rounding on the V side is the 2^-23 fixed point of P', and the
-// tensor core's accumulation adds none. Row k of the raw bytes minus its
-// masked row gives dim k (lo), the masked row / 16 dim k + 32.
+// the only rounding on the V side is the fixed point of P', and the tensor
+// core's accumulation adds none. Row k of the raw bytes minus its masked row
+// gives dim k (lo), the masked row / 16 dim k + 32.
 //
 // Softmax: base 2 with a lazy maximum per head that is uniform over the CTA
-// (a block whose score passes it by more than 8 moves it, decided by one
-// vote of the math warps); the integer accumulators cannot be rescaled, so a
-// move first adds them into f32 per-thread accumulators (rare: the first
-// block, and a handful afterwards).
+// (a block whose score passes it by more than kLazy = 2 moves it, decided by
+// one vote of the math warps), so p <= 4 and P' keeps 2^-30 of the block
+// maximum. Fixed point is absolute, not relative: every weight below half a
+// unit rounds to zero, so over 16384 positions up to 2^14 x 2^-30 of the
+// weight mass can be lost; with the threshold of 8 that the f16 kernel uses
+// (p <= 256, 2^-24) that was 1e-3 of the output at cfg5's length, above the
+// parity bar. The integer accumulators cannot be rescaled, so a move first
+// adds them into f32 per-thread accumulators (the first block, then rarely).
 //
 // Roles. Warps 0-3 (math), at block b: put the K rows of block b+1 into
 // tensor memory (buffer (b+1)%2) and load the K rows of block b+2 into
@@ -176,6 +180,9 @@ __device__ __forceinline__ float join4u(uint32_t d0, uint32_t d1, uint32_t d2, u
 }
 
 __device__ __forceinline__ float2 f2(float x) { return make_float2(x, x); }
+
+constexpr float kLazy = 2.0f;   // lazy-maximum threshold (log2 units): p <= 2^kLazy
+constexpr int kPFix = 29;       // P' fixed point: 2^kPFix units per unit of p * s_v * 2^(127 - vexp)
 
 // Exact f32 pair of the joined digit columns (d0 + 256 d1) + 65536 (d2 + 256 d3)
 // of two heads, as the other tensor-core kernel forms them.
@@ -479,7 +486,7 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
 #pragma unroll
   for (int i = 0; i < HH; i++) O[i] = 0.0f;
   const int vexp = min(max(vexp_raw, 1), 253);
-  const float fsx = pow2i(127 - vexp) * 8388608.0f;   // P' scale: 2^(127 - vexp) 2^23
+  const float fsx = pow2i(127 - vexp) * pow2i(kPFix);   // P' scale: 2^(127 - vexp) 2^kPFix
   float *red = reinterpret_cast<float *>(sm + C::RED);
   const int grp = (pos & 63) >> 5;   // group of this thread's output row
   // output accumulator columns of this thread: its row's group, its heads
@@ -536,7 +543,7 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
         for (int q = 0; q < HQ; q++) part[q] = f2(-INFINITY);
       }
     }
-    // lazy maximum: does any score pass its head's maximum by more than 8?
+    // lazy maximum: does any score pass its head's maximum by more than kLazy?
     float ex = -INFINITY;
 #pragma unroll
     for (int q = 0; q < HQ; q++) {
@@ -573,12 +580,12 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
       for (int i = 0; i < HH; i++) {
         const float bm = fmaxf(fmaxf(rw[i], rw[HH + i]), fmaxf(rw[2 * HH + i], rw[3 * HH + i]));
         float &m = (i & 1) ? M[i / 2].y : M[i / 2].x;
-        const bool need = bm > m + 8.0f;
+        const bool need = bm > m + kLazy;
         const float mn = need ? bm : m;
         const float al = need ? ex2(m - mn) : 1.0f;   // exp2(-inf) = 0
         m = mn;
         ((i & 1) ? NMEFF[i / 2].y : NMEFF[i / 2].x) = mn == -INFINITY ? 0.0f : -mn;
-        ((i & 1) ? NTHR[i / 2].y : NTHR[i / 2].x) = -(mn + 8.0f);
+        ((i & 1) ? NTHR[i / 2].y : NTHR[i / 2].x) = -(mn + kLazy);
         ((i & 1) ? L[i / 2].y : L[i / 2].x) *= al;
         ((i & 1) ? PB0[i / 2].y : PB0[i / 2].x) *= al;
         ((i & 1) ? PB1[i / 2].y : PB1[i / 2].x) *= al;
@@ -680,7 +687,7 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
     for (int i = 0; i < HH; i++) mh[h0 + i] = (i & 1) ? M[i / 2].y : M[i / 2].x;
   }
   __syncthreads();
-  const float oscale = pow2i(-23) * __uint_as_float((uint32_t)vexp << 23);   // 2^-23 2^(vexp-127)
+  const float oscale = pow2i(-kPFix) * __uint_as_float((uint32_t)vexp << 23);   // 2^-kPFix 2^(vexp-127)
   const size_t row0 = (size_t)(it.b * a.n_layers + it.lrow) * a.n_q_heads + qh0;
   for (int idx = t; idx < gh * HD; idx += C::NT) {
     const int h = idx / HD, d = idx - h * HD;

@@ -172,3 +172,22 @@ def test_cuda_core_kernel(shape):
     finally:
         E.force_path(0)
     check(name, "cuda-core kernel, planner splits", p, refs, qn, out)
+
+
+@pytest.mark.parametrize("longest", [False, True], ids=["planner", "longest"])
+def test_tcgen05_kernel(shape, longest):
+    """The tcgen05 formulation (exact s32 accumulation of the V side in
+    tensor memory, 32-bit fixed-point P'); head_dim 128 shapes only (others
+    keep the automatic choice and are covered above)."""
+    name, p, c, refs, qn, q = shape
+    if p["HD"] != 128:
+        pytest.skip("the tcgen05 kernel serves head_dim 128")
+    n = max(1, p["S"] // 64 // MAX_SPLIT_PAGES) if longest else 0
+    E.force_path(3)
+    E.force_splits(n)
+    try:
+        out = decode(c, q, p["NQ"])
+    finally:
+        E.force_path(0)
+        E.force_splits(0)
+    check(name, f"tcgen05 kernel, {'longest' if longest else 'planner'} splits", p, refs, qn, out)
