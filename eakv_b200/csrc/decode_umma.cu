@@ -114,11 +114,17 @@ struct UCfg {
   static constexpr int STAT = QS + RH * HD * 4;    // [RH] max|q|, [RH][NG] sums
   static_assert(STAT + RH * (1 + NG) * 4 <= OPP + NBUF * OPP_BYTES, "set-up scratch");
   // tensor memory columns
-  static constexpr int KOP = 0;                    // two K operand buffers: 16 raw, 16 masked columns
-  static constexpr int DS = 64;                    // two score buffers of 2 * NS columns
-  static constexpr int DV = DS + 4 * NS;           // outputs: NV columns
+  // K operands (16 raw, 16 masked columns) and scores (2 NS columns) are
+  // double-buffered at 8 heads (the next block's score MMAs are issued before
+  // this block's scores are read) and single at 4 heads, which then fits 128
+  // columns and three CTAs per SM (the next block is staged once this block's
+  // scores are in registers)
+  static constexpr bool DB = RH == 8;
+  static constexpr int KOP = 0;
+  static constexpr int DS = DB ? 64 : 32;
+  static constexpr int DV = DS + (DB ? 4 : 2) * NS;   // outputs: NV columns
   static constexpr int TCOLS = (DV + NV) <= 128 ? 128 : 256;
-  static constexpr int MINB = 2;                   // CTAs per SM
+  static constexpr int MINB = TCOLS == 128 ? 3 : 2;   // CTAs per SM
   static_assert(MINB * TCOLS <= 512, "tensor memory of the resident CTAs");
 };
 
@@ -379,18 +385,18 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
   auto issue_s = [&](int bb) {   // scores of block bb into score buffer bb % 2
     const uint64_t dq1 = sdesc(sb + C::QB1, 16, 512, kLayoutSW64);
     const uint64_t dq2 = sdesc(sb + C::QB2, 16, 512, kLayoutSW64);
-    const uint32_t ds = tb + C::DS + 2 * C::NS * (bb & 1);
+    const uint32_t ds = tb + C::DS + (C::DB ? 2 * C::NS * (bb & 1) : 0);
     fence_after_sync();
 #pragma unroll
     for (int g = 0; g < NG; g++) {
-      const uint32_t kop = tb + C::KOP + 32 * (bb & 1);
+      const uint32_t kop = tb + C::KOP + (C::DB ? 32 * (bb & 1) : 0);
       mma_i8_ts(ds + g * C::NS, kop + 8 * g, dq1 + 2 * g, id_s, 0u);
       mma_i8_ts(ds + g * C::NS, kop + 16 + 8 * g, dq2 + 2 * g, id_s, 1u);
     }
     // test hook: the completion of this block's scores is never signalled, so
     // the wait for it runs out
     if (2 * bb != a.test_stall - 1 && 2 * bb + 1 != a.test_stall - 1)
-      mma_commit(bar_s + 8 * (bb & 1));
+      mma_commit(bar_s + (C::DB ? 8 * (bb & 1) : 0));
   };
   auto issue_v = [&](int vbuf, bool acc) {   // V of the block in buffer vbuf
     const uint64_t dva = sdesc(sb + C::OPV + vbuf * C::OPV_BYTES, 8192, 512, kLayoutSW64);
@@ -445,7 +451,7 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
   // score MMAs
   float4 sk_next = rsk;
   auto stage_k = [&](int bb) {
-    const uint32_t kc = tb + lane_off + C::KOP + 32 * (bb & 1) + 4 * CPT * half;
+    const uint32_t kc = tb + lane_off + C::KOP + (C::DB ? 32 * (bb & 1) : 0) + 4 * CPT * half;
 #pragma unroll
     for (int c = 0; c < CPT; c++) {
       tmem_st4(kc + 4 * c, rk[c]);
@@ -510,21 +516,29 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
   int vbuf = 0;   // V and P buffers of block b
   for (int b = 0; math && b < nblk; b++) {
     const float4 sk = sk_next;
-    // K of block b+1 into its operand buffer (last read by S(b-1), complete),
-    // whose score MMAs then run while block b is finished; then the loads of
-    // block b+2's K rows
-    if (b + 1 < nblk) {
+    // double buffers: K of block b+1 into its operand buffer (last read by
+    // S(b-1), complete), whose score MMAs then run while block b is finished;
+    // then the loads of block b+2's K rows
+    if (C::DB && b + 1 < nblk) {
       stage_k(b + 1);
       if (b + 2 < nblk) load_k(b + 2);
     }
     // scores of block b (this thread's heads, both groups)
-    if (!mbar_wait_sleep(bar_s + 8 * (b & 1), (b >> 1) & 1, budget)) fail = true;
+    const bool s_ok = C::DB ? mbar_wait_sleep(bar_s + 8 * (b & 1), (b >> 1) & 1, budget)
+                            : mbar_wait_sleep(bar_s, b & 1, budget);
+    if (!s_ok) fail = true;
     fence_after_sync();
-    const uint32_t ds = tb + lane_off + C::DS + 2 * C::NS * (b & 1) + 4 * h0;
+    const uint32_t ds = tb + lane_off + C::DS + (C::DB ? 2 * C::NS * (b & 1) : 0) + 4 * h0;
     uint32_t d0[4 * HH], d1[4 * HH];   // (head, digit) columns of each group
     tmem_ldn<4 * HH>(ds, d0);
     tmem_ldn<4 * HH>(ds + C::NS, d1);
     tmem_wait_ld();
+    // single buffers: the K operands and the score columns are free again once
+    // S(b) has completed and its scores are in registers
+    if (!C::DB && b + 1 < nblk) {
+      stage_k(b + 1);
+      if (b + 2 < nblk) load_k(b + 2);
+    }
     float2 part[HQ];
 #pragma unroll
     for (int q = 0; q < HQ; q++) {
