@@ -74,15 +74,10 @@ template <int RH>
 struct UCfg {
   static constexpr int HD = 128;
   static constexpr int NG = 2;                     // groups per position
-  // threads per position of a block (two, each with half of the heads, were
-  // measured slower: the per-position costs are paid twice)
-  static constexpr int TPP = 1;
-  static constexpr int NM = 128 * TPP;             // math threads
+  static constexpr int NM = 128;                   // math threads: one per position of a block
   static constexpr int NW = NM / 32;               // math warps
   static constexpr int NT = NM + 32;               // + the control warp
-  static constexpr int HH = RH / TPP;              // query heads per thread
-  static constexpr int HQ = HH / 2;                // head pairs per thread
-  static constexpr int CPT = 4 / TPP;              // 16-byte chunks of a K / V row per thread
+  static constexpr int HQ = RH / 2;                // head pairs
   static constexpr int BLK = 128;                  // positions per block (two pages)
   static constexpr int NS = 4 * RH;                // score columns per group: (head, digit)
   static constexpr int NV = 8 * RH;                // output columns: (group, head, digit)
@@ -103,8 +98,8 @@ struct UCfg {
                        BAR_STAGED = BAR_DRAIN + 8, BAR_P = BAR_STAGED + 16;
   static constexpr int FLAGS = BAR_P + 16;         // [NBUF] accumulate flags of V(b)
   static constexpr int SLOT = FLAGS + 16;          // tensor-memory base address
-  static constexpr int RED = SLOT + 16;            // [NW warps][HH] floats
-  static constexpr int HCON = RED + ((NW * HH * 4 + 15) / 16) * 16;   // [RH] w, q sums g0, g1
+  static constexpr int RED = SLOT + 16;            // [NW warps][RH] floats
+  static constexpr int HCON = RED + ((NW * RH * 4 + 15) / 16) * 16;   // [RH] w, q sums g0, g1
   static constexpr int END = HCON + 3 * RH * 4;
   static_assert(BAR_S % 8 == 0 && BAR_P % 8 == 0 && SLOT % 8 == 0 && HCON % 16 == 0 &&
                 FLAGS + 4 * NBUF <= SLOT, "shared-memory alignment (mbarriers, float2 reads)");
@@ -211,16 +206,14 @@ template <int RH>
 __global__ void __launch_bounds__(UCfg<RH>::NT, UCfg<RH>::MINB)
 decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__ DecodeBatch batch) {
   using C = UCfg<RH>;
-  constexpr int HD = C::HD, NG = C::NG, HH = C::HH, HQ = C::HQ;
+  constexpr int HD = C::HD, NG = C::NG, HQ = C::HQ;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_s = smem_u32(smem_raw);
   const uint32_t sb = (raw_s + 1023u) & ~1023u;   // shared-space base, 1024-aligned
   uint8_t *sm = smem_raw + (sb - raw_s);
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const bool math = t < C::NM;                     // warp NW: the control warp
-  const int pos = t & 127, half = (t >> 7) & (C::TPP - 1);   // position, share of the heads
-  const int h0 = half * HH;                        // first query head of this thread
-  constexpr int CPT = C::CPT;
+  const int pos = t & 127;                         // position of the block (math threads)
   const int G = a.n_q_heads / a.geom.n_heads;
   const int gh = a.cta_heads;
   const int nhg = G / (gh > 0 ? gh : 1);
@@ -257,9 +250,9 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
   };
   if (warp == C::NW && lane < 4)
     for (int bb = 0; bb <= PF; bb++) prefetch_block(bb, lane);
-  // this thread's 16-byte chunks (CPT half ..) of a position's K or V row and
-  // the position's (scale, bias) pairs, loaded a step ahead
-  uint4 rk[CPT], rv[CPT];
+  // the four 16-byte chunks of this position's K or V row and its (scale,
+  // bias) pairs, loaded a step ahead
+  uint4 rk[4], rv[4];
   float4 rsk, rsv;
   auto row_ptr = [&](const uint8_t *pages, int bb) -> const uint8_t * {
     const int pi = 2 * bb + pp;
@@ -269,13 +262,13 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
     const uint8_t *kp = row_ptr(kpages, bb);
     if (kp) {
 #pragma unroll
-      for (int c = 0; c < CPT; c++) rk[c] = ldg_na(kp + prow * 64 + 16 * (CPT * half + c));
+      for (int c = 0; c < 4; c++) rk[c] = ldg_na(kp + prow * 64 + 16 * c);
       const uint4 s4 = ldg_na(kp + 4096 + prow * 16);
       rsk = make_float4(__uint_as_float(s4.x), __uint_as_float(s4.y), __uint_as_float(s4.z),
                         __uint_as_float(s4.w));
     } else {
 #pragma unroll
-      for (int c = 0; c < CPT; c++) rk[c] = make_uint4(0u, 0u, 0u, 0u);
+      for (int c = 0; c < 4; c++) rk[c] = make_uint4(0u, 0u, 0u, 0u);
       rsk = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
   };
@@ -283,13 +276,13 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
     const uint8_t *vp = row_ptr(vpages, bb);
     if (vp) {
 #pragma unroll
-      for (int c = 0; c < CPT; c++) rv[c] = ldg_na(vp + prow * 64 + 16 * (CPT * half + c));
+      for (int c = 0; c < 4; c++) rv[c] = ldg_na(vp + prow * 64 + 16 * c);
       const uint4 s4 = ldg_na(vp + 4096 + prow * 16);
       rsv = make_float4(__uint_as_float(s4.x), __uint_as_float(s4.y), __uint_as_float(s4.z),
                         __uint_as_float(s4.w));
     } else {
 #pragma unroll
-      for (int c = 0; c < CPT; c++) rv[c] = make_uint4(0u, 0u, 0u, 0u);
+      for (int c = 0; c < 4; c++) rv[c] = make_uint4(0u, 0u, 0u, 0u);
       rsv = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     }
   };
@@ -375,9 +368,9 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
   }
   fence_proxy_async_smem();
   __syncthreads();   // query digits and per-head constants in place
-  const float2 *W = reinterpret_cast<const float2 *>(hcon) + h0 / 2;
-  const float2 *QS0 = reinterpret_cast<const float2 *>(hcon + RH) + h0 / 2;
-  const float2 *QS1 = reinterpret_cast<const float2 *>(hcon + 2 * RH) + h0 / 2;
+  const float2 *W = reinterpret_cast<const float2 *>(hcon);
+  const float2 *QS0 = reinterpret_cast<const float2 *>(hcon + RH);
+  const float2 *QS1 = reinterpret_cast<const float2 *>(hcon + 2 * RH);
 
   // ---- the MMAs (issued by the control thread) ------------------------------------------
   const uint32_t id_s = idesc_i8(128, C::NS, 0, 1, 0, 0);
@@ -451,9 +444,9 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
   // score MMAs
   float4 sk_next = rsk;
   auto stage_k = [&](int bb) {
-    const uint32_t kc = tb + lane_off + C::KOP + (C::DB ? 32 * (bb & 1) : 0) + 4 * CPT * half;
+    const uint32_t kc = tb + lane_off + C::KOP + (C::DB ? 32 * (bb & 1) : 0);
 #pragma unroll
-    for (int c = 0; c < CPT; c++) {
+    for (int c = 0; c < 4; c++) {
       tmem_st4(kc + 4 * c, rk[c]);
       tmem_st4(kc + 16 + 4 * c, make_uint4(rk[c].x & 0xF0F0F0F0u, rk[c].y & 0xF0F0F0F0u,
                                            rk[c].z & 0xF0F0F0F0u, rk[c].w & 0xF0F0F0F0u));
@@ -464,14 +457,14 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
     __syncwarp();
     if (lane == 0) mbar_arrive(bar_staged + 8 * (bb & 1));
   };
-  uint32_t voff[CPT];
+  uint32_t voff[4];
 #pragma unroll
-  for (int c = 0; c < CPT; c++) voff[c] = swz_off(pos, 16 * (CPT * half + c), 64);
+  for (int c = 0; c < 4; c++) voff[c] = swz_off(pos, 16 * c, 64);
   // V chunks of this thread -> the block's shared buffer (raw rows, masked rows)
   auto stage_v = [&](int vbuf) {
     uint8_t *vr = sm + C::OPV + vbuf * C::OPV_BYTES;
 #pragma unroll
-    for (int c = 0; c < CPT; c++) {
+    for (int c = 0; c < 4; c++) {
       *reinterpret_cast<uint4 *>(vr + voff[c]) = rv[c];
       *reinterpret_cast<uint4 *>(vr + 8192 + voff[c]) =
           make_uint4(rv[c].x & 0xF0F0F0F0u, rv[c].y & 0xF0F0F0F0u, rv[c].z & 0xF0F0F0F0u,
@@ -479,9 +472,9 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
     }
   };
 
-  // ---- softmax state of this thread's heads ----------------------------------------------
+  // ---- softmax state, per head ------------------------------------------------------------
   float2 M[HQ], NMEFF[HQ], NTHR[HQ], L[HQ], PB0[HQ], PB1[HQ];
-  float O[HH];
+  float O[RH];
 #pragma unroll
   for (int q = 0; q < HQ; q++) {
     M[q] = f2(-INFINITY);
@@ -490,19 +483,19 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
     L[q] = PB0[q] = PB1[q] = f2(0.0f);
   }
 #pragma unroll
-  for (int i = 0; i < HH; i++) O[i] = 0.0f;
+  for (int i = 0; i < RH; i++) O[i] = 0.0f;
   const int vexp = min(max(vexp_raw, 1), 253);
   const float fsx = pow2i(127 - vexp) * pow2i(kPFix);   // P' scale: 2^(127 - vexp) 2^kPFix
   float *red = reinterpret_cast<float *>(sm + C::RED);
   const int grp = (pos & 63) >> 5;   // group of this thread's output row
-  // output accumulator columns of this thread: its row's group, its heads
-  const uint32_t dv_cols = tb + lane_off + C::DV + grp * 4 * RH + 4 * h0;
+  // output accumulator columns of this thread's row: its group's (head, digit)
+  const uint32_t dv_cols = tb + lane_off + C::DV + grp * 4 * RH;
   auto drain_dv = [&]() {   // adds the integer output accumulators to O
-    uint32_t d[4 * HH];
-    tmem_ldn<4 * HH>(dv_cols, d);
+    uint32_t d[4 * RH];
+    tmem_ldn<4 * RH>(dv_cols, d);
     tmem_wait_ld();
 #pragma unroll
-    for (int i = 0; i < HH; i++) O[i] += join4u(d[4 * i], d[4 * i + 1], d[4 * i + 2], d[4 * i + 3]);
+    for (int i = 0; i < RH; i++) O[i] += join4u(d[4 * i], d[4 * i + 1], d[4 * i + 2], d[4 * i + 3]);
   };
   auto vbar_wait = [&](int bb) {
     return mbar_wait_sleep(bar_v + 8 * (bb % C::NBUF), (bb / C::NBUF) & 1, budget);
@@ -523,15 +516,15 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
       stage_k(b + 1);
       if (b + 2 < nblk) load_k(b + 2);
     }
-    // scores of block b (this thread's heads, both groups)
+    // scores of block b (every head, both groups)
     const bool s_ok = C::DB ? mbar_wait_sleep(bar_s + 8 * (b & 1), (b >> 1) & 1, budget)
                             : mbar_wait_sleep(bar_s, b & 1, budget);
     if (!s_ok) fail = true;
     fence_after_sync();
-    const uint32_t ds = tb + lane_off + C::DS + (C::DB ? 2 * C::NS * (b & 1) : 0) + 4 * h0;
-    uint32_t d0[4 * HH], d1[4 * HH];   // (head, digit) columns of each group
-    tmem_ldn<4 * HH>(ds, d0);
-    tmem_ldn<4 * HH>(ds + C::NS, d1);
+    const uint32_t ds = tb + lane_off + C::DS + (C::DB ? 2 * C::NS * (b & 1) : 0);
+    uint32_t d0[4 * RH], d1[4 * RH];   // (head, digit) columns of each group
+    tmem_ldn<4 * RH>(ds, d0);
+    tmem_ldn<4 * RH>(ds + C::NS, d1);
     tmem_wait_ld();
     // single buffers: the K operands and the score columns are free again once
     // S(b) has completed and its scores are in registers
@@ -579,8 +572,8 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
           m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
         }
         if (lane == 0) {
-          red[warp * HH + 2 * q] = m0;
-          red[warp * HH + 2 * q + 1] = m1;
+          red[warp * RH + 2 * q] = m0;
+          red[warp * RH + 2 * q + 1] = m1;
         }
       }
       named_sync(1, C::NM);
@@ -589,10 +582,9 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
         fence_after_sync();
         drain_dv();
       }
-      const float *rw = red + (4 * half) * HH;   // the four warps of this share
 #pragma unroll
-      for (int i = 0; i < HH; i++) {
-        const float bm = fmaxf(fmaxf(rw[i], rw[HH + i]), fmaxf(rw[2 * HH + i], rw[3 * HH + i]));
+      for (int i = 0; i < RH; i++) {
+        const float bm = fmaxf(fmaxf(red[i], red[RH + i]), fmaxf(red[2 * RH + i], red[3 * RH + i]));
         float &m = (i & 1) ? M[i / 2].y : M[i / 2].x;
         const bool need = bm > m + kLazy;
         const float mn = need ? bm : m;
@@ -614,7 +606,7 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
     if (b + 1 < nblk) load_v(b + 1);
     // probabilities, bias sums and this thread's P digits of its position
     const float svx0 = sv.x * fsx, svx1 = sv.z * fsx;
-    uint32_t x0[HH], x1[HH];
+    uint32_t x0[RH], x1[RH];
 #pragma unroll
     for (int q = 0; q < HQ; q++) {
       const float2 x = __fadd2_rn(part[q], NMEFF[q]);
@@ -630,18 +622,12 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
     }
     // words (g, h) of the P row: group g at g RH + h
     uint8_t *pr = sm + C::OPP + vbuf * C::OPP_BYTES;
-    if constexpr (HH >= 4) {
 #pragma unroll
-      for (int c = 0; c < HH / 4; c++) {
-        *reinterpret_cast<uint4 *>(pr + swz_off(pos, 4 * h0 + 16 * c, C::PROW)) =
-            make_uint4(x0[4 * c], x0[4 * c + 1], x0[4 * c + 2], x0[4 * c + 3]);
-        *reinterpret_cast<uint4 *>(pr + swz_off(pos, 4 * (RH + h0) + 16 * c, C::PROW)) =
-            make_uint4(x1[4 * c], x1[4 * c + 1], x1[4 * c + 2], x1[4 * c + 3]);
-      }
-    } else {
-      *reinterpret_cast<uint2 *>(pr + swz_off(pos, 4 * h0, C::PROW)) = make_uint2(x0[0], x0[1]);
-      *reinterpret_cast<uint2 *>(pr + swz_off(pos, 4 * (RH + h0), C::PROW)) =
-          make_uint2(x1[0], x1[1]);
+    for (int c = 0; c < RH / 4; c++) {
+      *reinterpret_cast<uint4 *>(pr + swz_off(pos, 16 * c, C::PROW)) =
+          make_uint4(x0[4 * c], x0[4 * c + 1], x0[4 * c + 2], x0[4 * c + 3]);
+      *reinterpret_cast<uint4 *>(pr + swz_off(pos, 4 * RH + 16 * c, C::PROW)) =
+          make_uint4(x1[4 * c], x1[4 * c + 1], x1[4 * c + 2], x1[4 * c + 3]);
     }
     if (t == 0) vflags[vbuf] = vacc ? 1 : 0;   // V(b) accumulates onto earlier blocks
     fence_proxy_async_smem();
@@ -675,8 +661,8 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
   float *rl = ow + 128 * RH;                                    // [4 warps][RH]
   float *rpb = rl + 4 * RH;                                     // [4 warps][RH][NG]
 #pragma unroll
-  for (int i = 0; i < HH && math; i++) {
-    const int h = h0 + i, q = i / 2;
+  for (int i = 0; i < RH && math; i++) {
+    const int h = i, q = i / 2;
     ow[pos * RH + h] = O[i];
     float l = (i & 1) ? L[q].y : L[q].x;
     float p0 = (i & 1) ? PB0[q].y : PB0[q].x;
@@ -698,7 +684,7 @@ decode_umma_kernel(const __grid_constant__ DecodeArgs a, const __grid_constant__
   float *mh = rpb + 4 * RH * NG;                                // [RH]
   if (math && pos == 0) {
 #pragma unroll
-    for (int i = 0; i < HH; i++) mh[h0 + i] = (i & 1) ? M[i / 2].y : M[i / 2].x;
+    for (int i = 0; i < RH; i++) mh[i] = (i & 1) ? M[i / 2].y : M[i / 2].x;
   }
   __syncthreads();
   const float oscale = pow2i(-kPFix) * __uint_as_float((uint32_t)vexp << 23);   // 2^-kPFix 2^(vexp-127)
