@@ -44,15 +44,17 @@
 // adds them into f32 per-thread accumulators (the first block, then rarely).
 //
 // Roles. Warps 0-3 (math), at block b: put the K rows of block b+1 into
-// tensor memory (buffer (b+1)%2) and load the K rows of block b+2 into
-// registers; read the scores of block b; put its V rows into their shared
-// buffer b%3 and load the V rows of block b+1; run the softmax and write the
-// P digits of block b. The rows come from L2: the control thread prefetched
-// their pages a few blocks ahead with cp.async.bulk.prefetch. Warp 4
-// (control, one thread) issues the MMAs: S(b) as soon as block b's K rows
-// are in place (the scores are double-buffered, so S(b) runs while the math
-// warps work on block b-1), V(b) once block b's V rows and P digits are
-// written. They meet on mbarriers only (math warps arrive once per warp, the
+// tensor memory and load the K rows of block b+2 into registers; read the
+// scores of block b; put its V rows into their shared buffer b%3 and load
+// the V rows of block b+1; run the softmax and write the P digits of block
+// b. At 8 heads the K operands and scores are double-buffered and block
+// b+1's K goes in before block b's scores are read; at 4 heads they are
+// single and it goes in right after (128 tensor-memory columns, 3 CTAs per
+// SM). The rows come from L2: the control thread prefetched their pages a
+// few blocks ahead with cp.async.bulk.prefetch. Warp 4 (control, one thread)
+// issues the MMAs: S(b) as soon as block b's K rows are in place (so it runs
+// while the math warps finish block b-1), V(b) once block b's V rows and P
+// digits are written. They meet on mbarriers only (math warps arrive once per warp, the
 // MMAs complete on tcgen05.commit); every wait is bounded, suspends rather
 // than spins, and a wait that runs out makes the whole CTA leave through the
 // status word.
