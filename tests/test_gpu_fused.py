@@ -25,10 +25,15 @@ def _reset_splits():
 # "mma" the mma.sync tensor-core kernel and "umma" the tcgen05 kernel (shapes
 # a forced kernel does not serve fall back to the automatic choice)
 PATHS = ["auto", "simt", "mma", "umma"]
+# the two tensor-core formulations, for the edge cases below (the tcgen05 one
+# serves head_dim 128; its cases use that head_dim)
+TC_PATHS = ["auto", "umma"]
 
 
+@pytest.mark.parametrize("path", TC_PATHS)
 @pytest.mark.parametrize("name", ["mha128", "gqa64_8to2", "gqa128_4to1", "mha64"])
-def test_golden_fused(gpu, name):
+def test_golden_fused(gpu, name, path):
+    E.force_path(PATH_CODE[path])
     g = golden(f"attn_{name}.npz")
     L, nq, nkv, hd, S, maxS = [int(v) for v in g["shape"]]
     with E.Cache(L, nkv, hd, maxS) as c:
@@ -98,10 +103,12 @@ def test_large_scores_softmax_stability(gpu, path):
         assert_close(c.fused(q, 0, nq, nkv), rc.fused(q, 0, nq, nkv), what="sharp softmax")
 
 
-def test_decode_batch_ragged(gpu):
+@pytest.mark.parametrize("path,hd", [("auto", 64), ("umma", 128)])
+def test_decode_batch_ragged(gpu, path, hd):
     """Batched decode over caches of different lengths and every layer."""
     import torch
-    B, L, nq, nkv, hd, maxS = 5, 3, 16, 4, 64, 600
+    E.force_path(PATH_CODE[path])
+    B, L, nq, nkv, maxS = 5, 3, 16, 4, 600
     lens = [1, 64, 65, 333, 600]
     rng = np.random.default_rng(21)
     caches, refs = [], []
@@ -177,10 +184,12 @@ def test_decode_host_pipelined(gpu, shape, pinned):
         c.free()
 
 
-def test_partial_ranges_and_lse_combine(gpu):
+@pytest.mark.parametrize("path", TC_PATHS)
+def test_partial_ranges_and_lse_combine(gpu, path):
     """Sequence split across (simulated) ranks: partial outputs + LSE over
     disjoint position ranges, merged by eakv_lse_combine == full attention."""
     import torch
+    E.force_path(PATH_CODE[path])
     L, nq, nkv, hd, S = 2, 8, 2, 128, 1000
     rng = np.random.default_rng(33)
     data = kv_data(rng, L, nkv, S, hd)
@@ -218,16 +227,20 @@ def test_partial_ranges_and_lse_combine(gpu):
         assert torch.isneginf(lse[0]).all()
 
 
-def test_fused_empty_cache_is_nan(gpu):
+@pytest.mark.parametrize("path", TC_PATHS)
+def test_fused_empty_cache_is_nan(gpu, path):
     """seq_len 0: the reference's fused kernel divides 0 by a zero sum."""
+    E.force_path(PATH_CODE[path])
     with E.Cache(1, 2, 128, 64) as c:
         out = c.fused(np.ones(4 * 128, np.float32), 0, 4, 2)
         assert np.isnan(out).all()
 
 
-def test_restore_limits_attention(gpu):
+@pytest.mark.parametrize("path,hd", [("auto", 64), ("umma", 128)])
+def test_restore_limits_attention(gpu, path, hd):
     """After restore(n), attention sees exactly the first n positions."""
-    L, nq, nkv, hd, S = 1, 4, 4, 64, 300
+    E.force_path(PATH_CODE[path])
+    L, nq, nkv, S = 1, 4, 4, 300
     rng = np.random.default_rng(8)
     data = kv_data(rng, L, nkv, S, hd)
     rc = O.RefCache(L, nkv, hd, S)
@@ -244,10 +257,13 @@ def test_device_status_clean(gpu):
     assert E.device_status(0, reset=False) == 0
 
 
+@pytest.mark.parametrize("path", TC_PATHS)
 @pytest.mark.parametrize("vscale", [1e-30, 1e-3, 1.0, 1e4, 1e30])
-def test_extreme_value_scales(gpu, vscale):
+def test_extreme_value_scales(gpu, vscale, path):
     """V values over 60 orders of magnitude and a K/V range that grows
-    along the sequence: the tensor-core path rescales its f16 operands."""
+    along the sequence: the tensor-core paths rescale their P' operands
+    (f16 limbs, or the tcgen05 kernel's fixed point) by the V-scale exponent."""
+    E.force_path(PATH_CODE[path])
     L, nq, nkv, hd, S = 1, 16, 4, 128, 640
     rng = np.random.default_rng(int(np.log10(vscale)) + 100)
     data = kv_data(rng, L, nkv, S, hd)
@@ -263,9 +279,11 @@ def test_extreme_value_scales(gpu, vscale):
         assert_close(got / vscale, ref / vscale, what=f"V scale {vscale}")
 
 
+@pytest.mark.parametrize("path,hd", [("auto", 64), ("umma", 128)])
 @pytest.mark.parametrize("qscale", [1e-6, 1e-2, 1e3])
-def test_query_magnitudes(gpu, qscale):
-    L, nq, nkv, hd, S = 1, 32, 4, 64, 300
+def test_query_magnitudes(gpu, qscale, path, hd):
+    E.force_path(PATH_CODE[path])
+    L, nq, nkv, S = 1, 32, 4, 300
     rng = np.random.default_rng(5)
     data = kv_data(rng, L, nkv, S, hd)
     rc = O.RefCache(L, nkv, hd, S)
