@@ -211,7 +211,12 @@ constexpr int kVHeads = 8;          // query heads per block (accumulators per t
 constexpr int kVThreads = 128;
 constexpr int kVChunkPages = 8;     // positions of one block: 512
 constexpr int kVExactMax = 512;     // up to this length the whole sum is one chain
-constexpr int kVMergeInLaunch = 32; // most blocks per sequence merged inside the launch
+constexpr int kVMergeInLaunch = 64; // most blocks per sequence merged inside the launch
+
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+  return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z),
+                     __fadd_rn(a.w, b.w));
+}
 
 // A block's arrival at its item's counter, after its partial sums are
 // written: true in the item's last block to arrive. The counter wraps back
@@ -405,22 +410,25 @@ vsum_kernel(const uint8_t *__restrict__ buf, PageGeom g, int layer,
   }
   // the last block of this (KV head, head group) adds the blocks' sums in
   // chunk order (L1 bypassed: the other blocks wrote them from other SMs),
-  // eight loads in flight at a time
+  // four elements per thread and eight 16-byte loads in flight
   if (cnt && vsum_arrive_last(cnt + blockIdx.y * gridDim.z + blockIdx.z, n_chunks)) {
-    const size_t n = (size_t)n_q * HD;
-    for (int e = threadIdx.x; e < nh * HD; e += kVThreads) {
-      const float *pr = part + (size_t)(kvh * q_per_kv + h0) * HD + e;
-      float a = __ldcg(pr);
-      int c = 1;
-      for (; c + 8 <= n_chunks; c += 8) {
-        float v[8];
+    const size_t n4 = (size_t)n_q * HD / 4;   // float4 per chunk
+    const size_t row = (size_t)(kvh * q_per_kv + h0) * HD / 4;
+    const float4 *p4 = reinterpret_cast<const float4 *>(part) + row;
+    float4 *o4 = reinterpret_cast<float4 *>(out) + row;
+    for (int e = threadIdx.x; e < nh * HD / 4; e += kVThreads) {
+      float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      for (int c = 0; c < n_chunks; c += 8) {
+        const int m = min(8, n_chunks - c);
+        float4 v[8];
 #pragma unroll
-        for (int u = 0; u < 8; u++) v[u] = __ldcg(pr + (size_t)(c + u) * n);
+        for (int u = 0; u < 8; u++)
+          if (u < m) v[u] = __ldcg(p4 + (size_t)(c + u) * n4 + e);
 #pragma unroll
-        for (int u = 0; u < 8; u++) a = __fadd_rn(a, v[u]);
+        for (int u = 0; u < 8; u++)
+          if (u < m) a = (c + u == 0) ? v[u] : add4(a, v[u]);
       }
-      for (; c < n_chunks; c++) a = __fadd_rn(a, __ldcg(pr + (size_t)c * n));
-      out[(size_t)(kvh * q_per_kv + h0) * HD + e] = a;
+      o4[e] = a;
     }
   }
 }

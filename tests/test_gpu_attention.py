@@ -90,6 +90,17 @@ def test_chunked_v_sum(gpu, S, H, nq, nkv):
     cache's head count. The blocks meet at counters in the cache's workspace,
     which the fused decode uses too: a decode between two V-sums leaves the
     second one bit-identical to the first."""
+    chunked_case(S, H, nq, nkv)
+
+
+@pytest.mark.parametrize("S", [20000, 32768, 36000])
+def test_chunked_v_sum_many_blocks(gpu, S):
+    """Long sequences (8-page blocks): 40 and 64 blocks per sequence are
+    merged by the last block inside the launch, 71 by a second kernel."""
+    chunked_case(S, 8, 32, 8)
+
+
+def chunked_case(S, H, nq, nkv):
     L, hd = 1, 128
     rng = np.random.default_rng(S * 3 + nq)
     data = kv_data(rng, L, H, S, hd)
