@@ -410,12 +410,14 @@ vsum_kernel(const uint8_t *__restrict__ buf, PageGeom g, int layer,
   }
   // the last block of this (KV head, head group) adds the blocks' sums in
   // chunk order (L1 bypassed: the other blocks wrote them from other SMs),
-  // four elements per thread and eight 16-byte loads in flight
+  // four elements per thread and eight 16-byte loads in flight (the partial
+  // sums sit in the library's 256-byte aligned workspace; the output is the
+  // caller's buffer, written one float at a time)
   if (cnt && vsum_arrive_last(cnt + blockIdx.y * gridDim.z + blockIdx.z, n_chunks)) {
     const size_t n4 = (size_t)n_q * HD / 4;   // float4 per chunk
     const size_t row = (size_t)(kvh * q_per_kv + h0) * HD / 4;
     const float4 *p4 = reinterpret_cast<const float4 *>(part) + row;
-    float4 *o4 = reinterpret_cast<float4 *>(out) + row;
+    float *o = out + row * 4;
     for (int e = threadIdx.x; e < nh * HD / 4; e += kVThreads) {
       float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       for (int c = 0; c < n_chunks; c += 8) {
@@ -428,7 +430,10 @@ vsum_kernel(const uint8_t *__restrict__ buf, PageGeom g, int layer,
         for (int u = 0; u < 8; u++)
           if (u < m) a = (c + u == 0) ? v[u] : add4(a, v[u]);
       }
-      o4[e] = a;
+      o[4 * e] = a.x;
+      o[4 * e + 1] = a.y;
+      o[4 * e + 2] = a.z;
+      o[4 * e + 3] = a.w;
     }
   }
 }

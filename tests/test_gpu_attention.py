@@ -100,6 +100,30 @@ def test_chunked_v_sum_many_blocks(gpu, S):
     chunked_case(S, 8, 32, 8)
 
 
+@pytest.mark.parametrize("S", [20000, 36000])
+def test_v_sum_device_buffers_at_any_float_offset(gpu, S):
+    """The device V-sum takes the caller's weight and output buffers at any
+    4-byte offset (here one float past a 256-byte boundary), with the blocks'
+    sums merged inside the launch (40 blocks) or by a second kernel (71), and
+    equals the host-buffer call bit for bit."""
+    import torch
+    L, H, nq, nkv, hd = 1, 8, 32, 8, 128
+    rng = np.random.default_rng(S + 5)
+    data = kv_data(rng, L, H, S, hd)
+    with E.Cache(L, H, hd, S) as c:
+        assert c.load_raw(data, S) == 0
+        w = rng.random(nq * S, dtype=np.float32) / S
+        want = c.output(w, 0, nq, nkv)
+        wbuf = torch.zeros(nq * S + 1, device=gpu)
+        wbuf[1:] = torch.from_numpy(w).to(gpu)
+        obuf = torch.full((nq * hd + 1,), float("nan"), device=gpu)
+        torch.cuda.synchronize()   # the cache runs on its own stream
+        c.output_device(wbuf[1:], 0, nq, nkv, obuf[1:])
+        c.synchronize()
+        assert np.array_equal(bits(obuf[1:].cpu().numpy()), bits(want))
+    assert E.device_status(0) == 0
+
+
 def chunked_case(S, H, nq, nkv):
     L, hd = 1, 128
     rng = np.random.default_rng(S * 3 + nq)
