@@ -376,14 +376,25 @@ vsum_kernel(const uint8_t *__restrict__ buf, PageGeom g, int layer,
   float *dst = n_chunks == 1 ? out : part + (size_t)blockIdx.x * n_q * HD;
   if (nused == 1) {
     if (stream == 0) {
+      // dst is the caller's buffer when the call is one block: 16-byte
+      // stores only where it is 16-byte aligned
+      const bool vec = ((uintptr_t)dst & 15) == 0;
 #pragma unroll
       for (int j = 0; j < NH; j++) {
         if (j < nh) {
           float *r = dst + (size_t)(kvh * q_per_kv + h0 + j) * HD + dim0;
-          *reinterpret_cast<float4 *>(r) =
-              make_float4(o[j][0].x, o[j][0].y, o[j][1].x, o[j][1].y);
-          *reinterpret_cast<float4 *>(r + 32) =
-              make_float4(o[j][2].x, o[j][2].y, o[j][3].x, o[j][3].y);
+          if (vec) {
+            *reinterpret_cast<float4 *>(r) =
+                make_float4(o[j][0].x, o[j][0].y, o[j][1].x, o[j][1].y);
+            *reinterpret_cast<float4 *>(r + 32) =
+                make_float4(o[j][2].x, o[j][2].y, o[j][3].x, o[j][3].y);
+          } else {
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+              r[(k >> 1) * 32 + 2 * (k & 1)] = o[j][k].x;
+              r[(k >> 1) * 32 + 2 * (k & 1) + 1] = o[j][k].y;
+            }
+          }
         }
       }
     }

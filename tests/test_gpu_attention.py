@@ -100,12 +100,13 @@ def test_chunked_v_sum_many_blocks(gpu, S):
     chunked_case(S, 8, 32, 8)
 
 
-@pytest.mark.parametrize("S", [20000, 36000])
+@pytest.mark.parametrize("S", [300, 1000, 20000, 36000])
 def test_v_sum_device_buffers_at_any_float_offset(gpu, S):
     """The device V-sum takes the caller's weight and output buffers at any
-    4-byte offset (here one float past a 256-byte boundary), with the blocks'
-    sums merged inside the launch (40 blocks) or by a second kernel (71), and
-    equals the host-buffer call bit for bit."""
+    4-byte offset (here one float past a 256-byte boundary): one block
+    writing the output itself (300 positions), the blocks' sums merged inside
+    the launch (16 and 40 blocks) or by a second kernel (71); it equals the
+    host-buffer call bit for bit."""
     import torch
     L, H, nq, nkv, hd = 1, 8, 32, 8, 128
     rng = np.random.default_rng(S + 5)
