@@ -212,10 +212,38 @@ constexpr int kVThreads = 128;
 constexpr int kVChunkPages = 8;     // positions of one block: 512
 constexpr int kVExactMax = 512;     // up to this length the whole sum is one chain
 constexpr int kVMergeInLaunch = 64; // most blocks per sequence merged inside the launch
+constexpr int kVRun = 8;            // blocks per run of the two-level merge
+static_assert(kVMergeInLaunch <= kVRun * kVRun, "the second merge level adds at most kVRun runs");
 
 __device__ __forceinline__ float4 add4(float4 a, float4 b) {
   return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z),
                      __fadd_rn(a.w, b.w));
+}
+
+// dst[e] = src[0][e] + src[stride][e] + ... (n <= kVRun terms, in that
+// order) for the float4 columns e of one (KV head, head group): all n loads
+// of a column in flight at once, L1 bypassed (other blocks wrote them).
+// dst4 (16-byte aligned) or, when it is null, dst (any 4-byte offset).
+__device__ __forceinline__ void vsum_add_run(const float4 *src, size_t stride, int n, int cols,
+                                             float4 *dst4, float *dst) {
+  for (int e = threadIdx.x; e < cols; e += kVThreads) {
+    float4 v[kVRun];
+#pragma unroll
+    for (int u = 0; u < kVRun; u++)
+      if (u < n) v[u] = __ldcg(src + (size_t)u * stride + e);
+    float4 a = v[0];
+#pragma unroll
+    for (int u = 1; u < kVRun; u++)
+      if (u < n) a = add4(a, v[u]);
+    if (dst4) {
+      dst4[e] = a;
+    } else {
+      dst[4 * e] = a.x;
+      dst[4 * e + 1] = a.y;
+      dst[4 * e + 2] = a.z;
+      dst[4 * e + 3] = a.w;
+    }
+  }
 }
 
 // A block's arrival at its item's counter, after its partial sums are
@@ -300,9 +328,14 @@ vsum_kernel(const uint8_t *__restrict__ buf, PageGeom g, int layer,
       if (status) atomicOr(status, kStatusWaitTimeout);
       mbar_wait(smem_u32(bar), 0, kWaitBudget);   // no copy may outlive the block
     }
-    // arrive all the same, so that the counter returns to zero (the status
+    // arrive all the same, so that the counters return to zero (the status
     // word tells the caller the result is void)
-    if (cnt) vsum_arrive_last(cnt + blockIdx.y * gridDim.z + blockIdx.z, n_chunks);
+    if (cnt) {
+      const int n_run = (n_chunks + kVRun - 1) / kVRun, run = blockIdx.x / kVRun;
+      unsigned *gc = cnt + (size_t)(blockIdx.y * gridDim.z + blockIdx.z) * (n_run + 1);
+      if (vsum_arrive_last(gc + 1 + run, min(kVRun, n_chunks - run * kVRun)) && n_run > 1)
+        vsum_arrive_last(gc, n_run);
+    }
     return;
   }
   const int stream = threadIdx.x / TPS, i = threadIdx.x - stream * TPS;
@@ -419,32 +452,30 @@ vsum_kernel(const uint8_t *__restrict__ buf, PageGeom g, int layer,
     for (int st = 1; st < NSTREAM; st++) a = __fadd_rn(a, acc_s[(st * nh + j) * HD + d]);
     dst[(size_t)(kvh * q_per_kv + h0 + j) * HD + d] = a;
   }
-  // the last block of this (KV head, head group) adds the blocks' sums in
-  // chunk order (L1 bypassed: the other blocks wrote them from other SMs),
-  // four elements per thread and eight 16-byte loads in flight (the partial
-  // sums sit in the library's 256-byte aligned workspace; the output is the
-  // caller's buffer, written one float at a time)
-  if (cnt && vsum_arrive_last(cnt + blockIdx.y * gridDim.z + blockIdx.z, n_chunks)) {
-    const size_t n4 = (size_t)n_q * HD / 4;   // float4 per chunk
-    const size_t row = (size_t)(kvh * q_per_kv + h0) * HD / 4;
-    const float4 *p4 = reinterpret_cast<const float4 *>(part) + row;
-    float *o = out + row * 4;
-    for (int e = threadIdx.x; e < nh * HD / 4; e += kVThreads) {
-      float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      for (int c = 0; c < n_chunks; c += 8) {
-        const int m = min(8, n_chunks - c);
-        float4 v[8];
-#pragma unroll
-        for (int u = 0; u < 8; u++)
-          if (u < m) v[u] = __ldcg(p4 + (size_t)(c + u) * n4 + e);
-#pragma unroll
-        for (int u = 0; u < 8; u++)
-          if (u < m) a = (c + u == 0) ? v[u] : add4(a, v[u]);
+  // Blocks' sums, two levels, in chunk order: the last block of each run of
+  // kVRun blocks adds the run's sums into the run's first slot (or, for a
+  // single run, into the output); the last run to finish adds the runs'
+  // sums into the output. Each level is one round of loads from L2 per
+  // column (the partial sums sit in the library's 256-byte aligned
+  // workspace; the output is the caller's buffer, written one float at a
+  // time).
+  if (cnt) {
+    const int n_run = (n_chunks + kVRun - 1) / kVRun, run = blockIdx.x / kVRun;
+    unsigned *gc = cnt + (size_t)(blockIdx.y * gridDim.z + blockIdx.z) * (n_run + 1);
+    const int r0 = run * kVRun, rn = min(kVRun, n_chunks - r0);
+    if (vsum_arrive_last(gc + 1 + run, rn)) {
+      const size_t n4 = (size_t)n_q * HD / 4;   // float4 per chunk
+      const size_t row = (size_t)(kvh * q_per_kv + h0) * HD / 4;
+      const float4 *p4 = reinterpret_cast<const float4 *>(part) + row;
+      const int cols = nh * HD / 4;
+      if (n_run == 1) {
+        vsum_add_run(p4, n4, rn, cols, nullptr, out + row * 4);
+      } else {
+        vsum_add_run(p4 + (size_t)r0 * n4, n4, rn, cols,
+                     reinterpret_cast<float4 *>(part) + row + (size_t)r0 * n4, nullptr);
+        if (vsum_arrive_last(gc, n_run))
+          vsum_add_run(p4, (size_t)kVRun * n4, n_run, cols, nullptr, out + row * 4);
       }
-      o[4 * e] = a.x;
-      o[4 * e + 1] = a.y;
-      o[4 * e + 2] = a.z;
-      o[4 * e + 3] = a.w;
     }
   }
 }
@@ -578,8 +609,9 @@ size_t vsum_scratch_floats(const PageGeom &g, int n_q, int n_kv, int seq_len) {
 
 size_t vsum_counters(int n_q, int n_kv, int seq_len) {
   const int n_chunks = vsum_chunks(n_q, n_kv, seq_len);
+  const int n_run = (n_chunks + kVRun - 1) / kVRun;
   return n_chunks > 1 && n_chunks <= kVMergeInLaunch
-             ? (size_t)n_kv * ((n_q / n_kv + kVHeads - 1) / kVHeads) : 0;
+             ? (size_t)n_kv * ((n_q / n_kv + kVHeads - 1) / kVHeads) * (n_run + 1) : 0;
 }
 
 cudaError_t launch_vsum(const PageGeom &g, const uint8_t *d_buf, int layer, const float *d_w,
