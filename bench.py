@@ -28,6 +28,7 @@ per thread, on a bounded sample of the workload.
 import argparse
 import json
 import os
+import platform
 import statistics
 import subprocess
 import sys
@@ -217,6 +218,33 @@ def cpu_reference(cfg, threads, seconds, seed=0):
     return tps, sample, kind
 
 
+def cpu_model():
+    """The host CPU's model name (first /proc/cpuinfo entry), for the record."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return platform.processor() or "unknown"
+
+
+def cpu_reference_pinned(cfg, seconds):
+    """cpu_reference on one thread pinned to one core of this process's set
+    (the affinity is restored afterwards)."""
+    try:
+        old = os.sched_getaffinity(0)
+        os.sched_setaffinity(0, {min(old)})
+    except (AttributeError, OSError):
+        old = None
+    try:
+        return cpu_reference(cfg, 1, seconds)
+    finally:
+        if old is not None:
+            os.sched_setaffinity(0, old)
+
+
 def softmax_f32(scores, nq, S):
     s = scores.reshape(nq, S)
     m = np.maximum(s.max(axis=1, keepdims=True), np.float32(-1e6))
@@ -268,6 +296,7 @@ def run_reference(args, cfg, world, rank):
         "data": "synthetic (seeded N(0,1) K/V, per-channel log-uniform[0.5,8] K scale)",
         "config": config_json(cfg, world), "impl": "reference",
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+                         "cpu": cpu_model(),
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -583,8 +612,9 @@ def run_b200(args, cfg, world, rank, local):
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu:
-            tps, sample, kind = cpu_reference(cfg, 1, args.cpu_seconds)
-            cpu = {"value": tps, "unit": UNIT, "cores": 1, "kind": kind, "sample": sample}
+            tps, sample, kind = cpu_reference_pinned(cfg, args.cpu_seconds)
+            cpu = {"value": tps, "unit": UNIT, "cores": 1, "kind": kind, "sample": sample,
+                   "cpu": cpu_model(), "pinned": True}
         result = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
