@@ -208,7 +208,7 @@ struct HostStreams {
   cudaStream_t in = nullptr, out = nullptr, alt = nullptr;
   cudaStream_t coll = nullptr;   // collectives and merges of the multi-GPU split
 };
-constexpr size_t kPipelineMinBytes = 1u << 20;
+constexpr size_t kPipelineMinBytes = 1u << 18;
 int host_streams(int dev, HostStreams &hs);
 int host_chunks(int n, int (&start)[5]);
 // decode_mma.cu: tensor-core decode, any number of query heads per KV head

@@ -115,7 +115,7 @@ int eakv_decode_attention_noalloc(const eakv_cache_t *const *caches,
                                   int n_caches, const float *d_queries,
                                   int n_q_heads, float *d_output, void *stream);
 /* Same with host buffers; copies in, decodes, copies out, synchronizes.
- * From 1 MiB of queries on, the batch is cut into up to four chunks of
+ * From 256 KiB of queries on, the batch is cut into up to four chunks of
  * caches (or of layers, for one cache) whose copies overlap the other
  * chunks' decodes; every chunk keeps the whole batch's split plan, so the
  * outputs equal eakv_decode_attention's bit for bit. */

@@ -141,7 +141,7 @@ def test_decode_batch_ragged(gpu, path, hd):
 @pytest.mark.parametrize("shape", ["by_cache", "by_layer"])
 @pytest.mark.parametrize("pinned", [False, True])
 def test_decode_host_pipelined(gpu, shape, pinned):
-    """At 1 MiB of queries and more, the host-buffer decode runs in chunks
+    """At 256 KiB of queries and more, the host-buffer decode runs in chunks
     (caches, or the layers of a single cache) whose copies overlap the
     other chunks' decodes; every chunk keeps the whole batch's split plan,
     so the outputs equal the device-buffer form's bit for bit."""

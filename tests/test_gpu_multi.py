@@ -77,7 +77,7 @@ def _worker(rank, world, port, hs, lens, L, result_q):
             stream.synchronize()
             outs.append(do.cpu().numpy())
         assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
-        # the host-buffer form (chunked from 1 MiB of queries on) gives the same bits
+        # the host-buffer form (chunked from 256 KiB of queries on) gives the same bits
         hq = np.ascontiguousarray(q[:, :, h_i * qh:(h_i + 1) * qh])
         ho = np.full_like(hq, np.nan)
         dist.barrier()
